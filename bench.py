@@ -1,0 +1,445 @@
+"""Decode-step benchmark of the kavor_b200 Qwen3 path (BASELINE config 3 headline).
+
+Workload: Qwen3-8B (random-init bf16, the reference checkpoint shapes), a
+decode batch of 256 sequences whose context is 1024 tokens (block_size 256),
+tensor parallel over the N GPUs of the launch (TP=N, one process per GPU,
+NCCL). A step = one decode step of the whole batch: embedding, 36 layers,
+LM head and sampling, replayed from the captured CUDA graph.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Printed on rank 0 as one JSON line:
+* value / ms_per_step: device time (CUDA events, max over ranks) of K graph
+  replays with the batch metadata already resident in HBM;
+* e2e: the same metric through the public per-step API ModelRunner.run (host
+  metadata build, one pinned host->device copy, graph replay, sampled token ids
+  read back to the host), sequences growing by one token per step;
+* roofline: the decode-attention kernel (dominant kernel: its K/V bytes are
+  ~70% of the step's HBM bytes at TP1) timed alone over the layers' caches;
+* step_roofline: whole-step HBM bytes (weights + KV) at the measured peak;
+* cpu_baseline: the CPU oracle (reference algorithm) timed on the host cores;
+* clocks: nvidia-smi samples taken during the timed region.
+``--impl reference`` times the reference algorithm on the host CPU (the
+oracle restatement; the reference's own GPU path needs flash-attn/Triton
+kernels that are not part of this build) and prints the same line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="Qwen3-8B")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--context", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ----------------------------------------------------------------- helpers
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def model_shape(name: str) -> dict:
+    from kavor_b200.config import QWEN3_PRESETS
+
+    d = dict(QWEN3_PRESETS[name])
+    d["vocab_size"] = 151936
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi samples (100 ms) of the SM clock and throttle reasons while running."""
+
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, index: int):
+        self.lines: list[str] = []
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], 0.0, set()
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, f[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def max_over_ranks(x: float) -> float:
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def barrier():
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+# ----------------------------------------------------------------- CPU reference path
+class CpuDecodeSample:
+    """The CPU oracle (the reference algorithm restated on the CPU) on one decode
+    step of the workload: one decoder layer at the full batch and context, and
+    the LM-head GEMM; a step's time is extrapolated as num_layers x layer +
+    head. Weight / KV values are cheap deterministic fills (the timing does not
+    depend on them)."""
+
+    def __init__(self, shape: dict, batch: int, context: int, threads: int):
+        sys.path.insert(0, str(ROOT))
+        from oracle import model as om
+        from oracle import ops
+
+        self.om, self.ops = om, ops
+        torch.set_num_threads(threads)
+        self.layers = shape["num_hidden_layers"]
+        H, I = shape["hidden_size"], shape["intermediate_size"]
+        hq, hkv, hd = shape["num_attention_heads"], shape["num_key_value_heads"], 128
+
+        def fill(*s):
+            n = math.prod(s)
+            return ((torch.arange(n, dtype=torch.int32) % 251 - 125).to(torch.bfloat16) * 1e-4).view(*s)
+
+        pre = "model.layers.0."
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16)  # noqa: E731
+        self.p = {pre + "self_attn.q_proj.weight": fill(hq * hd, H), pre + "self_attn.k_proj.weight": fill(hkv * hd, H),
+                  pre + "self_attn.v_proj.weight": fill(hkv * hd, H), pre + "self_attn.o_proj.weight": fill(H, hq * hd),
+                  pre + "mlp.gate_proj.weight": fill(I, H), pre + "mlp.up_proj.weight": fill(I, H),
+                  pre + "mlp.down_proj.weight": fill(H, I), pre + "self_attn.q_norm.weight": ones(hd),
+                  pre + "self_attn.k_norm.weight": ones(hd), pre + "input_layernorm.weight": ones(H),
+                  pre + "post_attention_layernorm.weight": ones(H)}
+        nb = (context + 255) // 256
+        self.pool = fill(batch * nb, 2, 256, hkv, hd)
+        tables = torch.arange(batch * nb, dtype=torch.int32).view(batch, nb)
+        ctx = torch.full((batch,), context, dtype=torch.int32)
+        pos = torch.full((batch,), context - 1)
+        slots = tables[:, (context - 1) // 256] * 256 + (context - 1) % 256
+        self.batch = om.Batch(False, pos, slots, context_lens=ctx, block_tables=tables)
+        self.cache = ops.cos_sin_cache(hd, context + 1, 1e6)
+        self.shape = om.Shape(hidden=H, inter=I, layers=1, hq=hq, hkv=hkv)
+        self.h = fill(batch, H) * 100
+        self.layer()  # warm-up
+        head_w = fill(shape["vocab_size"], H)
+        t0 = time.perf_counter()
+        ops.linear(self.h, head_w)
+        self.t_head = time.perf_counter() - t0
+
+    def layer(self) -> float:
+        t0 = time.perf_counter()
+        self.om.decoder_layer(self.p, 0, self.h, self.h.clone(), self.batch, (self.pool[:, 0], self.pool[:, 1]),
+                              self.shape, self.cache)
+        return time.perf_counter() - t0
+
+    def step_time(self) -> float:
+        """One sampled decode step: one timed layer, extrapolated to all layers + head."""
+        return self.layers * self.layer() + self.t_head
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0  # the CPU reference runs once, on rank 0
+    shape = model_shape(args.model)
+    threads = os.cpu_count() or 1
+    sample = CpuDecodeSample(shape, args.batch, args.context, threads)
+    for _ in range(args.warmup):
+        sample.step_time()
+    steps = [sample.step_time() for _ in range(args.steps)]
+    t_step = sum(steps) / len(steps)
+    value = args.batch / t_step
+    sample = (f"each step: 1 of {shape['num_hidden_layers']} decoder layers + the LM head of one decode step "
+              f"(B={args.batch}, ctx={args.context}) on the CPU oracle, extrapolated x{shape['num_hidden_layers']}")
+    line = {
+        "impl": "reference", "metric": f"decode output tok/s ({args.model}, B={args.batch}, ctx={args.context})",
+        "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "config": _config(args),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference algorithm restated on the host CPU (oracle/); the reference's own GPU kernels "
+                "(flash-attn, Triton) are third-party and not part of this build",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _config(args) -> dict:
+    return {"workload": f"{args.model} decode step, batch {args.batch}, context {args.context}, TP={args.gpus}",
+            "model": args.model, "global_batch": args.batch, "context": args.context, "block_size": 256,
+            "parallelism": f"tp{args.gpus}",
+            "l2": "inputs larger than L2 (per step: all weights + every sequence's KV pages)"}
+
+
+# ----------------------------------------------------------------- our path
+def step_bytes(shape: dict, tp: int, batch: int, context: int) -> int:
+    """Algorithmic HBM bytes of one decode step per rank: every weight once,
+    every context token's K/V once, the new K/V rows written, embedding rows."""
+    H, I, L = shape["hidden_size"], shape["intermediate_size"], shape["num_hidden_layers"]
+    hq, hkv, hd = shape["num_attention_heads"] // tp, shape["num_key_value_heads"] // tp, 128
+    per_layer = H * (hq + 2 * hkv) * hd + hq * hd * H + 3 * H * (I // tp)
+    weights = 2 * (L * per_layer + (shape["vocab_size"] // tp) * H)
+    kv = L * batch * (context * 2 * hkv * hd * 2 + 2 * hkv * hd * 2)
+    return weights + kv + 2 * batch * H
+
+
+def attention_bytes(batch: int, context: int, hq: int, hkv: int) -> int:
+    """Algorithmic bytes of one decode-attention launch: K and V of every
+    context token once, q read and o written."""
+    return batch * context * hkv * 128 * 2 * 2 + 2 * batch * hq * 128 * 2
+
+
+def run_ours(args) -> int:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+    else:
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_free_port()}", world_size=1, rank=0,
+                                device_id=dev)
+
+    from kavor_b200 import _kernels as K
+    from kavor_b200 import _lib
+    from kavor_b200.config import Config, write_model_dir
+    from kavor_b200.engine.block_manager import BlockManager
+    from kavor_b200.engine.model_runner import ModelRunner
+    from kavor_b200.engine.sequence import Sequence
+    from kavor_b200.sampling_params import SamplingParams
+
+    shape = model_shape(args.model)
+    B, ctx0 = args.batch, args.context
+    extra = args.warmup + args.steps + 2
+    max_len = ((ctx0 + 2 * extra + 255) // 256 + 1) * 256
+    blocks_per_seq = (ctx0 + 2 * extra + 255) // 256
+    tmp = tempfile.mkdtemp(prefix="kvb_bench_")
+    model_dir = write_model_dir(os.path.join(tmp, f"r{rank}"), args.model)
+    cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world, max_model_len=max_len,
+                 max_num_seqs=B, max_num_batched_tokens=4096, num_kvcache_blocks=B * blocks_per_seq + 8,
+                 rdzv_port=1)
+    runner = ModelRunner(cfg, rank, None)
+    with torch.no_grad():
+        runner.cache.pools.view(torch.bfloat16).normal_(0.0, 1.0)  # resident KV pages, N(0, 1)
+
+    Sequence.block_size = 256
+    bm = BlockManager(cfg.num_kvcache_blocks, 256, enable_prefix_cache=False)
+    g = torch.Generator().manual_seed(0)
+    seqs = []
+    for _ in range(B):
+        s = Sequence(torch.randint(0, 151936, (ctx0,), generator=g).tolist(),
+                     SamplingParams(temperature=0.6, max_tokens=10 ** 6, ignore_eos=True))
+        bm.allocate_prefill(s, 0)
+        s.num_cached_tokens = ctx0 - 1  # KV of the first ctx0-1 tokens is resident
+        s.is_prefill = False
+        seqs.append(s)
+
+    hq, hkv = shape["num_attention_heads"] // world, shape["num_key_value_heads"] // world
+    bucket = next(b for b in runner.graph_bs if b >= B)
+    graph = runner.graphs[bucket]
+
+    # --- device-timed decode steps (metadata resident: every step repeats context ctx0)
+    runner.run(seqs, False)  # fills the graph's static inputs for context ctx0
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    t_dev = max_over_ranks(start.elapsed_time(end) / 1e3)
+    clk = clocks.stop()
+    ms_per_step = t_dev / args.steps * 1e3
+    value = B * args.steps / t_dev
+    launches = runner.graph_launches.get(bucket, 0) * args.steps
+
+    # --- decode attention alone, rotating over the layers' caches (no L2 reuse)
+    attn = [m for m in runner.model.modules() if hasattr(m, "k_cache") and hasattr(m, "v_cache")]
+    d = runner.decode_buffers.d
+    q = torch.randn(B, hq, 128, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(q)
+    bt, cl = d["block_tables"][:B], d["context_lens"][:B]
+
+    def attn_launch(i):
+        a = attn[i % len(attn)]
+        K.paged_decode_attention(q, a.k_cache[0], a.v_cache[0], bt, cl, 128 ** -0.5, out=out)
+
+    for i in range(3):
+        attn_launch(i)
+    torch.cuda.synchronize()
+    n_attn = 2 * len(attn)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n_attn):
+        attn_launch(i)
+    e1.record()
+    torch.cuda.synchronize()
+    t_attn = max_over_ranks(e0.elapsed_time(e1) / 1e3 / n_attn)
+    ctx_now = int(cl[0].item())
+    a_bytes = attention_bytes(B, ctx_now, hq, hkv)
+    peak, peak_src = measured_peaks()
+    prof = ROOT / "profiles" / "decode_attention_traffic.json"
+    traffic = None
+    if prof.exists():
+        tr = json.loads(prof.read_text())
+        key = f"{args.model}_B{B}_ctx{ctx0}_tp{world}"
+        traffic = tr.get(key)
+    achieved = a_bytes / t_attn / 1e9
+    roofline = {"kernel": "decode_attn_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                "algorithmic_bytes": a_bytes, "avg_launch_us": t_attn * 1e6}
+    s_bytes = step_bytes(shape, world, B, ctx0)
+    t_roof = s_bytes / (peak * 1e9)
+    step_roof = {"bytes_per_rank": s_bytes, "t_hbm_us": t_roof * 1e6, "frac": t_roof / (ms_per_step / 1e3),
+                 "peak_gbs": peak, "peak_source": peak_src}
+
+    # --- end to end through ModelRunner.run (sequences advance one token per step)
+    e2e = None
+    if not args.no_e2e:
+        def e2e_step():
+            for s in seqs:
+                bm.may_append_block(s)
+            toks = runner.run(seqs, False)
+            for s, t in zip(seqs, toks):
+                s.num_cached_tokens += 1
+                s.append_token(t)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        f1.record()
+        torch.cuda.synchronize()
+        barrier()
+        t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+        e2e = {"value": B * args.steps / t_e2e, "unit": "tok/s", "ms_per_step": t_e2e / args.steps * 1e3,
+               "h2d_bytes_per_step": runner.decode_buffers.nbytes, "d2h_bytes_per_step": 8 * B,
+               "api": "ModelRunner.run(seqs, is_prefill=False)"}
+
+    dev_err = _lib.device_error(clear=True)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sample = CpuDecodeSample(shape, B, ctx0, threads)
+        t_step = statistics.median(sample.step_time() for _ in range(5))
+        cpu = {"value": B / t_step, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"5 sampled decode steps (B={B}, ctx={ctx0}): each 1 timed decoder layer of "
+                         f"{shape['num_hidden_layers']} + 1 LM-head GEMM on the CPU oracle, extrapolated "
+                         f"x{shape['num_hidden_layers']}",
+               "ms_per_step": t_step * 1e3}
+
+    if rank == 0:
+        line = {
+            "metric": f"decode output tok/s ({args.model}, B={B}, ctx={ctx0})", "value": value, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init weights (reference checkpoint shapes), random token ids, KV pages N(0,1)",
+            "config": _config(args), "decode_step_us": ms_per_step * 1e3, "attn_hbm_gbs": achieved,
+            "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": launches, "device_error_bits": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+    runner.graphs.clear()
+    runner.graph_pool = None
+    torch.cuda.synchronize()
+    barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

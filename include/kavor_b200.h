@@ -1,0 +1,187 @@
+/*
+ * kavor_b200 — C ABI of the B200 (sm_100a) kernels behind Kavor's Qwen3
+ * tensor-parallel decode/prefill path.
+ *
+ * Conventions shared by every entry point
+ *   - Pointers are device pointers unless stated otherwise. Activations and the
+ *     KV cache are bf16, metadata is int32 (slot_mapping, block_tables,
+ *     context_lens, cu_seqlens) or int64 (token ids, positions), exactly the
+ *     dtypes Kavor's ModelRunner builds (model_runner.py:434-473).
+ *   - Strides are in ELEMENTS, sizes are element or row counts.
+ *   - `stream` is a cudaStream_t passed as void*. Nothing is synchronised and
+ *     nothing is allocated inside a call; all of them can be captured in a CUDA
+ *     graph. Scratch memory is provided by the caller (query *_workspace_size).
+ *   - Return value: 0 = ok, <0 = invalid argument (checked on the host, nothing
+ *     launched), >0 = cudaError_t of the launch. kvb_last_error() gives the
+ *     message of the calling thread's last failure.
+ *   - Paged KV cache layout (cache_pool.py:311-322): one page per block and
+ *     layer, K block [block_size, num_kv_heads, head_dim] followed by the V
+ *     block; `block_stride` is the element distance between consecutive K
+ *     blocks (= 2 * block_size * num_kv_heads * head_dim), v_cache = k_cache +
+ *     block_size * num_kv_heads * head_dim.
+ */
+#ifndef KAVOR_B200_H
+#define KAVOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; only this API is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ------------------------------------------------------------------ library */
+
+/* ABI version (major*10000 + minor*100 + patch). */
+int kvb_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* kvb_last_error(void);
+
+/* OR of the device-side error bits raised by kernels on the CURRENT device
+ * since the last clear (1: block table, 2: slot, 4: wait timeout, 8: token id,
+ * 16: peer wait timeout). Synchronises the device. Returns 0 or a CUDA error. */
+int kvb_device_error(unsigned* bits, int clear);
+
+/* Number of SMs of the current device (used by the host-side heuristics). */
+int kvb_sm_count(int* out);
+
+/* ------------------------------------------------------------ KV-cache write */
+
+/* store_kvcache (flash_attention_kvcache.py:10-46): for every token t with
+ * slot_mapping[t] != -1, copy key[t] and value[t] ([num_kv_heads, head_dim],
+ * row strides key_stride/value_stride) into block slot/block_size, row
+ * slot%block_size of the paged cache. Slots >= num_blocks*block_size raise the
+ * device slot error and are skipped. */
+int kvb_store_kv(const void* key, int64_t key_stride, const void* value, int64_t value_stride,
+                 void* k_cache, void* v_cache, int64_t num_blocks, int64_t block_stride, int block_size,
+                 int num_kv_heads, int head_dim, const int32_t* slot_mapping, int num_tokens, void* stream);
+
+/* -------------------------------------------------------------- norms / RoPE */
+
+/* RMSNorm (layernorm.py:8-39, RMSNorm.rms_forward :319-342):
+ *   out = bf16( bf16(x * rsqrt(mean(x^2) + eps)) * weight ), fp32 inside.
+ * x/out are [tokens, heads, n_cols] with arbitrary token/head strides (heads=1
+ * with stride_h ignored for 2-D inputs); the last dimension is contiguous. */
+int kvb_rmsnorm(const void* x, int64_t x_stride_t, int64_t x_stride_h, void* out, int64_t out_stride_t,
+                int64_t out_stride_h, const void* weight, int tokens, int heads, int n_cols, float eps,
+                void* stream);
+
+/* Fused residual add + RMSNorm (layernorm.py:114-140, add_rms_forward :344-372):
+ *   r = fp32(x) + fp32(residual); residual <- bf16(r) (in place);
+ *   out = bf16( bf16(r * rsqrt(mean(r^2) + eps)) * weight ).
+ * x, residual, out are contiguous [tokens, n_cols]. out may alias x. */
+int kvb_add_rmsnorm(const void* x, void* residual, void* out, const void* weight, int tokens, int n_cols,
+                    float eps, void* stream);
+
+/* In-place rotary embedding of q and k (rotary_embedding.py:8-53, :104-120).
+ * cos_sin is the fp32 [max_position, head_dim] table [cos | sin] built as in
+ * rotary_embedding.py:96-102; interleaved selects (2i, 2i+1) pairs instead of
+ * (i, i + head_dim/2). Positions outside [0, max_position) are clamped and
+ * raise no error (the reference does not check them either). */
+int kvb_rope(void* q, int64_t q_stride_t, int64_t q_stride_h, void* k, int64_t k_stride_t,
+             int64_t k_stride_h, const int64_t* positions, const float* cos_sin, int64_t max_position,
+             int tokens, int q_heads, int k_heads, int head_dim, int interleaved, void* stream);
+
+/* Fused Qwen3 attention prologue (qwen3.py:80-89 + flash_attention_kvcache.py:72):
+ * on the packed qkv rows [tokens, (Hq + 2*Hkv) * head_dim] (row stride
+ * qkv_stride), in place: q_norm and k_norm (RMSNorm over head_dim, weights
+ * q_weight/k_weight), RoPE on q and k, then the k and v rows are written into
+ * the paged cache at slot_mapping (skipped for -1). apply_norm = 0 skips the
+ * norms (attention_bias models); k_cache = NULL skips the cache write. */
+int kvb_qknorm_rope_store(void* qkv, int64_t qkv_stride, int tokens, int num_q_heads, int num_kv_heads,
+                          int head_dim, const void* q_weight, const void* k_weight, float eps, int apply_norm,
+                          const int64_t* positions, const float* cos_sin, int64_t max_position, int interleaved,
+                          void* k_cache, void* v_cache, int64_t num_blocks, int64_t block_stride,
+                          int block_size, const int32_t* slot_mapping, void* stream);
+
+/* -------------------------------------------------------------- activation */
+
+/* SiluAndMul (activation.py:8-11): out[t, i] = bf16(silu(x[t, i]) * x[t, inter + i]),
+ * fp32 inside, one rounding. */
+int kvb_silu_mul(const void* x, int64_t x_stride, void* out, int64_t out_stride, int tokens, int inter,
+                 void* stream);
+
+/* ---------------------------------------------------------------- embedding */
+
+/* VocabParallelEmbedding lookup (embed_head.py:34-42 without the all-reduce):
+ * out[t] = weight[ids[t] - vocab_start] if vocab_start <= ids[t] < vocab_end,
+ * else zeros. weight is [vocab_end - vocab_start, hidden], out [tokens, hidden].
+ * vocab_size > 0 raises the device token-id error for ids outside [0, vocab_size). */
+int kvb_embedding(const int64_t* ids, const void* weight, void* out, int tokens, int hidden, int64_t vocab_start,
+                  int64_t vocab_end, int64_t vocab_size, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/* Bytes of scratch kvb_paged_decode_attn needs for this shape and split count
+ * (num_splits = 0 means the heuristic the call itself would pick). */
+int kvb_paged_decode_attn_workspace_size(int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                         int max_blocks_per_seq, int block_size, int num_splits,
+                                         size_t* bytes);
+
+/* Single-token decode attention over the paged cache
+ * (flash_attention_kvcache.py:80-83 = flash_attn_with_kvcache(q.unsqueeze(1),
+ * k_cache, v_cache, cache_seqlens=context_lens, block_table, causal=True)).
+ * q/out are [batch, num_q_heads, head_dim]; query head h reads kv head
+ * h / (num_q_heads / num_kv_heads). Rows with context_lens = 0 produce zeros.
+ * K/V blocks are staged into shared memory with TMA; the context is split
+ * across CTAs (num_splits; 0 = heuristic) and merged in a second kernel
+ * through `workspace` (>= kvb_paged_decode_attn_workspace_size bytes). */
+int kvb_paged_decode_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache,
+                          const void* v_cache, int64_t num_blocks, int64_t block_stride, int block_size,
+                          const int32_t* block_tables, int64_t block_table_stride, int max_blocks_per_seq,
+                          const int32_t* context_lens, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                          int batch, int num_q_heads, int num_kv_heads, int head_dim, float scale,
+                          int num_splits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal varlen prefill attention (flash_attention_kvcache.py:73-79 =
+ * flash_attn_varlen_func(..., causal=True, block_table)). Sequence b owns
+ * queries [cu_seqlens_q[b], cu_seqlens_q[b+1]) and attends keys
+ * [0, cu_seqlens_k[b+1] - cu_seqlens_k[b]) with bottom-right causal alignment.
+ * Keys come from the paged cache through block_tables (prefix cache / chunked
+ * prefill) when block_tables != NULL, else from the contiguous k/v rows
+ * [cu_seqlens_k[b] + j] (k_stride_t/h, v_stride_t/h). q/out [total_q, Hq, hd]. */
+int kvb_prefill_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                     int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                     int64_t num_blocks, int64_t block_stride, int block_size, const int32_t* block_tables,
+                     int64_t block_table_stride, int max_blocks_per_seq, const int32_t* cu_seqlens_q,
+                     const int32_t* cu_seqlens_k, int batch, int max_seqlen_q, void* out, int64_t out_stride_t,
+                     int64_t out_stride_h, int num_q_heads, int num_kv_heads, int head_dim, float scale,
+                     void* stream);
+
+/* ------------------------------------------------------------------ sampler */
+
+/* Sampler (sampler.py:7-66): token[b] = argmax_v(logits[b, v] / T[b] + g(b, v))
+ * with Gumbel noise g from Philox4x32-10 keyed by *seed (device int32) and
+ * counter b*vocab + v; T[b] == 0 is greedy argmax. Ties pick the lowest index.
+ * logits bf16 [batch, vocab] with row stride; out int64 [batch]. The seed is
+ * read, not advanced (the caller advances it, as sampler.py:59 does). */
+int kvb_sample(const void* logits, int64_t row_stride, const float* temperatures, const int32_t* seed,
+               int64_t* out, int batch, int vocab, void* stream);
+
+/* Vocab-sharded sampler for ParallelLMHead (embed_head.py:56-66): the same
+ * score over this rank's columns [vocab_offset, vocab_offset + shard_vocab)
+ * of a vocab_total-wide row, written as (best score, global index) pairs to
+ * best_val[b] / best_idx[b]. kvb_sample_combine then reduces world_size such
+ * pairs per row (gathered as [world_size, batch]) to the token ids. The result
+ * is identical to kvb_sample on the concatenated logits. */
+int kvb_sample_partial(const void* logits, int64_t row_stride, const float* temperatures, const int32_t* seed,
+                       float* best_val, int64_t* best_idx, int batch, int shard_vocab, int64_t vocab_offset,
+                       int64_t vocab_total, void* stream);
+int kvb_sample_combine(const float* vals, const int64_t* idxs, int world_size, int64_t* out, int batch,
+                       void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KAVOR_B200_H */

@@ -1,0 +1,89 @@
+"""Engine configuration (drop-in for kavor/config.py:16-53, text models).
+
+Extra fields over the reference: ``load_format`` ("auto" reads the checkpoint
+in ``model``, "dummy" draws a seeded random checkpoint of the same shapes),
+``seed`` for that draw, and ``enable_prefix_caching`` (the reference always
+caches prefixes).
+"""
+from __future__ import annotations
+
+import json
+import os
+import socket
+from dataclasses import dataclass
+from typing import Any
+
+
+def free_port() -> int:
+    if env := os.environ.get("KAVOR_RDZV_PORT"):
+        return int(env)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def load_hf_config(model_dir: str):
+    """Text config of a Qwen3-family model directory (transformers' own parser)."""
+    from transformers import AutoConfig
+
+    return AutoConfig.from_pretrained(model_dir, trust_remote_code=False)
+
+
+@dataclass(slots=True)
+class Config:
+    model: str
+    max_num_batched_tokens: int = 16384
+    max_num_seqs: int = 512
+    max_model_len: int = 4096
+    gpu_memory_utilization: float = 0.9
+    tensor_parallel_size: int = 1
+    enforce_eager: bool = False
+    profile: bool = False
+    trust_remote_code: bool = False
+    hf_config: Any = None
+    eos: int = -1
+    kvcache_block_size: int = 256
+    num_kvcache_blocks: int = -1
+    rdzv_port: int = -1
+    load_format: str = "auto"
+    seed: int = 0
+    enable_prefix_caching: bool = True
+
+    def __post_init__(self):
+        if not os.path.isdir(self.model):
+            raise RuntimeError(f"Model not found: {self.model}")
+        assert self.kvcache_block_size % 256 == 0, "kvcache_block_size must be a multiple of 256"
+        assert 1 <= self.tensor_parallel_size <= 8
+        assert self.load_format in ("auto", "dummy")
+        self.rdzv_port = self.rdzv_port if self.rdzv_port > 0 else free_port()
+        if self.hf_config is None:
+            self.hf_config = load_hf_config(self.model)
+        self.max_model_len = min(self.max_model_len, self.hf_config.max_position_embeddings)
+
+    @property
+    def text_config(self):
+        return self.hf_config
+
+
+# Shapes of the Qwen3 dense models used by the benchmarks (config.json fields).
+QWEN3_PRESETS: dict[str, dict] = {
+    "Qwen3-0.6B": dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
+                       num_key_value_heads=8, head_dim=128, tie_word_embeddings=True),
+    "Qwen3-8B": dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                     num_key_value_heads=8, head_dim=128, tie_word_embeddings=False),
+    "Qwen3-32B": dict(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64, num_attention_heads=64,
+                      num_key_value_heads=8, head_dim=128, tie_word_embeddings=False),
+}
+
+
+def write_model_dir(path: str, preset: str, **overrides) -> str:
+    """Write a weight-less model directory (config.json only) for load_format='dummy'."""
+    cfg = dict(architectures=["Qwen3ForCausalLM"], model_type="qwen3", vocab_size=151936,
+               max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1000000.0, hidden_act="silu",
+               attention_bias=False, torch_dtype="bfloat16", bos_token_id=151643, eos_token_id=151645)
+    cfg.update(QWEN3_PRESETS[preset])
+    cfg.update(overrides)
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    return path

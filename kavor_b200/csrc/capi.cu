@@ -1,0 +1,61 @@
+// Library-level entry points: version, error reporting, device queries.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "../../include/kavor_b200.h"
+
+namespace kvb {
+
+static thread_local char t_last_error[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return kOk;
+  set_error((int)e, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+  return (int)e;
+}
+
+// Error-word readers defined by each kernel translation unit.
+int read_device_error_elementwise(unsigned*, int);
+int read_device_error_decode(unsigned*, int);
+int read_device_error_prefill(unsigned*, int);
+int read_device_error_sampler(unsigned*, int);
+
+}  // namespace kvb
+
+extern "C" int kvb_version(void) { return 100; }
+
+extern "C" const char* kvb_last_error(void) { return kvb::t_last_error; }
+
+extern "C" int kvb_device_error(unsigned* bits, int clear) {
+  if (!bits) return kvb::set_error(kvb::kInvalid, "kvb_device_error: bits is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return kvb::cuda_status(e, "kvb_device_error: synchronize");
+  unsigned acc = 0, w = 0;
+  int (*readers[])(unsigned*, int) = {kvb::read_device_error_elementwise, kvb::read_device_error_decode,
+                                      kvb::read_device_error_prefill, kvb::read_device_error_sampler};
+  for (auto fn : readers) {
+    int rc = fn(&w, clear);
+    if (rc) return rc;
+    acc |= w;
+  }
+  *bits = acc;
+  return kvb::kOk;
+}
+
+extern "C" int kvb_sm_count(int* out) {
+  if (!out) return kvb::set_error(kvb::kInvalid, "kvb_sm_count: out is NULL");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return kvb::cuda_status(e, "kvb_sm_count: cudaGetDevice");
+  e = cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev);
+  return kvb::cuda_status(e, "kvb_sm_count: attribute");
+}

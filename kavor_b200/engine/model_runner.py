@@ -1,0 +1,423 @@
+"""Model runner (drop-in for kavor/engine/model_runner.py, Qwen3 text path).
+
+Per step (model_runner.py:247-262): build the batch metadata on the host,
+send it to the device in ONE pinned host->device copy, run the forward (a
+captured CUDA graph for decode buckets, eager for prefill), sample on the
+device and read the token ids back.
+
+Tensor parallelism: one process per GPU over NCCL. Two launch modes:
+* spawned by ``LLMEngine`` (rank 0 drives ranks > 0 through a shared-memory
+  mailbox, model_runner.py:51-112);
+* SPMD under an external launcher (torchrun): the process group already
+  exists and every rank calls ``run`` itself with the same sequences.
+Every rank computes the same sampled tokens (only (score, index) pairs cross
+ranks, see ParallelLMHead.sample), so the LM head and the sampler stay inside
+the decode graph at every TP size.
+"""
+from __future__ import annotations
+
+import os
+import pickle
+from multiprocessing.shared_memory import SharedMemory
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from kavor_b200 import _kernels as K
+from kavor_b200 import _lib
+from kavor_b200.engine.cache_pool import CachePool
+from kavor_b200.engine.sequence import Sequence
+from kavor_b200.layers.sampler import Sampler
+from kavor_b200.models import AutoModelForCausalLM
+from kavor_b200.utils.context import reset_context, set_context
+
+SHM_BYTES = 1 << 22
+
+
+# ----------------------------------------------------------------- host metadata
+def block_table_matrix(seqs: list[Sequence], width: int | None = None) -> np.ndarray:
+    """[B, max blocks] int32, rows padded with -1 (model_runner.py:469-473)."""
+    w = max(len(s.block_table) for s in seqs) if width is None else width
+    out = np.full((len(seqs), w), -1, dtype=np.int32)
+    for i, s in enumerate(seqs):
+        out[i, :len(s.block_table)] = s.block_table
+    return out
+
+
+def decode_metadata(seqs: list[Sequence], block_size: int) -> dict[str, np.ndarray]:
+    """model_runner.py:448-467: the last token of every sequence at position len-1,
+    written to slot block_table[-1]*block_size + last_block_num_tokens - 1."""
+    n = len(seqs)
+    return {
+        "input_ids": np.fromiter((s.last_token for s in seqs), np.int64, n),
+        "positions": np.fromiter((len(s) - 1 for s in seqs), np.int64, n),
+        "slot_mapping": np.fromiter(
+            (s.block_table[-1] * block_size + s.last_block_num_tokens - 1 for s in seqs), np.int32, n),
+        "context_lens": np.fromiter((len(s) for s in seqs), np.int32, n),
+        "block_tables": block_table_matrix(seqs),
+    }
+
+
+def prefill_metadata(seqs: list[Sequence], block_size: int) -> dict:
+    """model_runner.py:385-446: tokens [num_cached, num_cached + num_scheduled) of
+    every sequence, cumulative q/k lengths, slots through the block table, and
+    the block tables only when some keys come from the cache (prefix hit or a
+    later prefill chunk)."""
+    ids, pos, slots = [], [], []
+    cu_q, cu_k = [0], [0]
+    max_q = max_k = 0
+    for s in seqs:
+        start = s.num_cached_tokens
+        end = start + s.num_scheduled_tokens
+        ids.append(np.asarray(s.token_ids[start:end], dtype=np.int64))
+        t = np.arange(start, end, dtype=np.int64)
+        pos.append(t)
+        cu_q.append(cu_q[-1] + end - start)
+        cu_k.append(cu_k[-1] + end)
+        max_q = max(max_q, end - start)
+        max_k = max(max_k, end)
+        if s.block_table:
+            table = np.asarray(s.block_table, dtype=np.int64)
+            slots.append((table[t // block_size] * block_size + t % block_size).astype(np.int32))
+    meta = {
+        "input_ids": np.concatenate(ids) if ids else np.zeros(0, np.int64),
+        "positions": np.concatenate(pos) if pos else np.zeros(0, np.int64),
+        "cu_seqlens_q": np.asarray(cu_q, dtype=np.int32),
+        "cu_seqlens_k": np.asarray(cu_k, dtype=np.int32),
+        "max_seqlen_q": max_q,
+        "max_seqlen_k": max_k,
+        "slot_mapping": np.concatenate(slots) if slots else np.zeros(0, np.int32),
+        "block_tables": block_table_matrix(seqs) if cu_k[-1] > cu_q[-1] else None,
+    }
+    return meta
+
+
+# ----------------------------------------------------------------- staging
+class Staging:
+    """Pinned host area + device area; the arrays of one step are packed at
+    16-byte aligned offsets and cross PCIe in a single copy."""
+
+    def __init__(self, device: torch.device, capacity: int = 1 << 20):
+        self.device = device
+        self._grow(capacity)
+
+    def _grow(self, nbytes: int) -> None:
+        self.host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        self.dev = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+
+    def upload(self, arrays: list[np.ndarray]) -> list[torch.Tensor]:
+        offs, total = [], 0
+        for a in arrays:
+            offs.append(total)
+            total += (a.nbytes + 15) & ~15
+        if total > self.host.numel():
+            torch.cuda.current_stream().synchronize()
+            self._grow(max(total, 2 * self.host.numel()))
+        hv = self.host.numpy()
+        for a, o in zip(arrays, offs):
+            hv[o:o + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+        self.dev[:total].copy_(self.host[:total], non_blocking=True)
+        return [self.dev[o:o + a.nbytes].view(torch.from_numpy(a[:0]).dtype).view(a.shape)
+                for a, o in zip(arrays, offs)]
+
+
+class DecodeBuffers:
+    """Static device inputs of the decode graphs (fixed addresses) with a pinned
+    host mirror; one copy per step moves all of them."""
+
+    FIELDS = (("input_ids", np.int64), ("positions", np.int64), ("temperatures", np.float32),
+              ("slot_mapping", np.int32), ("context_lens", np.int32))
+
+    def __init__(self, max_bs: int, max_blocks: int, device: torch.device):
+        self.max_bs, self.max_blocks = max_bs, max_blocks
+        layout, off = {}, 0
+        for name, dt in self.FIELDS:
+            layout[name] = (off, dt, (max_bs,))
+            off += (max_bs * np.dtype(dt).itemsize + 15) & ~15
+        layout["block_tables"] = (off, np.int32, (max_bs, max_blocks))
+        off += max_bs * max_blocks * 4
+        self.nbytes = off
+        self.host = torch.zeros(off, dtype=torch.uint8, pin_memory=True)
+        self.dev = torch.zeros(off, dtype=torch.uint8, device=device)
+        self.h, self.d = {}, {}
+        hv = self.host.numpy()
+        for name, (o, dt, shape) in layout.items():
+            n = int(np.prod(shape)) * np.dtype(dt).itemsize
+            self.h[name] = hv[o:o + n].view(dt).reshape(shape)
+            self.d[name] = self.dev[o:o + n].view(torch.from_numpy(np.zeros(0, dt)).dtype).view(shape)
+        self.sampled = torch.zeros(max_bs, dtype=torch.int64, device=device)
+
+    def fill(self, meta: dict, temperatures: np.ndarray, bucket: int) -> None:
+        n = meta["input_ids"].shape[0]
+        h = self.h
+        h["input_ids"][:n] = meta["input_ids"]
+        h["input_ids"][n:bucket] = 0
+        h["positions"][:n] = meta["positions"]
+        h["positions"][n:bucket] = 0
+        h["temperatures"][:n] = temperatures
+        h["temperatures"][n:bucket] = 1.0
+        h["slot_mapping"][:n] = meta["slot_mapping"]
+        h["slot_mapping"][n:bucket] = -1
+        h["context_lens"][:n] = meta["context_lens"]
+        h["context_lens"][n:bucket] = 0
+        bt = meta["block_tables"]
+        h["block_tables"][:n, :bt.shape[1]] = bt
+        h["block_tables"][:n, bt.shape[1]:] = -1
+        self.dev.copy_(self.host, non_blocking=True)
+
+
+# ----------------------------------------------------------------- runner
+class ModelRunner:
+
+    def __init__(self, config, rank: int, event=None):
+        self.config = config
+        self.block_size = config.kvcache_block_size
+        self.enforce_eager = config.enforce_eager
+        self.world_size = config.tensor_parallel_size
+        self.rank = rank
+        self.event = event
+        self.shm = None
+        self.owns_process_group = False
+        if not dist.is_initialized():
+            dist.init_process_group("nccl", f"tcp://127.0.0.1:{config.rdzv_port}", world_size=self.world_size,
+                                    rank=rank, device_id=torch.device(f"cuda:{self._local_device(rank)}"))
+            self.owns_process_group = True
+        if dist.get_world_size() != self.world_size:
+            raise RuntimeError(f"process group has {dist.get_world_size()} ranks, config asks for {self.world_size}")
+        self.device = torch.device("cuda", self._local_device(rank))
+        torch.cuda.set_device(self.device)
+        prev_dtype = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        torch.set_default_device(self.device)
+        try:
+            Sequence.block_size = config.kvcache_block_size
+            self.model = AutoModelForCausalLM.from_pretrained(config.hf_config, load_format=config.load_format,
+                                                              seed=config.seed)
+            self.sampler = Sampler()
+            self.staging = Staging(self.device)
+            self.allocate_kv_cache()
+            self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+            self.graph_pool = None
+            if not self.enforce_eager:
+                self.capture_cudagraph()
+        finally:
+            torch.set_default_device("cpu")
+            torch.set_default_dtype(prev_dtype)
+        if self.world_size > 1 and event is not None:
+            self._open_mailbox()
+
+    @staticmethod
+    def _local_device(rank: int) -> int:
+        if "LOCAL_RANK" in os.environ:
+            return int(os.environ["LOCAL_RANK"])
+        return rank % max(1, torch.cuda.device_count())
+
+    # ------------------------------------------------------------ TP mailbox
+    def _mailbox_name(self) -> str:
+        return f"kavor_b200_{self.config.rdzv_port}"
+
+    def _open_mailbox(self) -> None:
+        name = self._mailbox_name()
+        if self.rank == 0:
+            try:
+                stale = SharedMemory(name=name)
+                stale.close()
+                stale.unlink()
+            except FileNotFoundError:
+                pass
+            self.shm = SharedMemory(name=name, create=True, size=SHM_BYTES)
+            dist.barrier()
+        else:
+            dist.barrier()
+            self.shm = SharedMemory(name=name)
+            self.loop()
+
+    def loop(self) -> None:
+        while True:
+            method, args = self.read_shm()
+            self.call(method, *args)
+            if method == "exit":
+                break
+
+    def read_shm(self):
+        self.event.wait()
+        n = int.from_bytes(self.shm.buf[0:4], "little")
+        method, *args = pickle.loads(self.shm.buf[4:n + 4])
+        self.event.clear()
+        return method, args
+
+    def write_shm(self, method: str, *args) -> None:
+        data = pickle.dumps([method, *args])
+        if len(data) + 4 > len(self.shm.buf):
+            raise RuntimeError(f"TP message of {len(data)} bytes exceeds the {len(self.shm.buf)}-byte mailbox")
+        self.shm.buf[0:4] = len(data).to_bytes(4, "little")
+        self.shm.buf[4:len(data) + 4] = data
+        for ev in self.event:
+            ev.set()
+
+    def call(self, method: str, *args):
+        if self.world_size > 1 and self.rank == 0 and self.shm is not None:
+            self.write_shm(method, *args)
+        return getattr(self, method)(*args)
+
+    def exit(self) -> None:
+        if self.shm is not None:
+            self.shm.close()
+            dist.barrier()
+            if self.rank == 0:
+                self.shm.unlink()
+            self.shm = None
+        self.graphs.clear()
+        self.graph_pool = None
+        torch.cuda.synchronize()
+        if self.owns_process_group and dist.is_initialized():
+            dist.destroy_process_group()
+
+    # ------------------------------------------------------------ KV pool
+    def _max_graph_bs(self) -> int:
+        return min(self.config.max_num_seqs, 512)
+
+    @property
+    def max_blocks_per_seq(self) -> int:
+        return (self.config.max_model_len + self.block_size - 1) // self.block_size
+
+    @torch.inference_mode()
+    def _profile_prefill(self) -> None:
+        seq_len = min(self.config.max_num_batched_tokens, self.config.max_model_len)
+        num_seqs = max(1, min(self.config.max_num_batched_tokens // seq_len, self.config.max_num_seqs))
+        total = seq_len * num_seqs
+        ids = torch.zeros(total, dtype=torch.int64, device=self.device)
+        pos = torch.arange(seq_len, device=self.device).repeat(num_seqs)
+        cu = torch.arange(0, total + 1, seq_len, dtype=torch.int32, device=self.device)
+        set_context(True, cu, cu, seq_len, seq_len, torch.zeros(total, dtype=torch.int32, device=self.device))
+        try:
+            hidden = self.model(ids, pos)
+            temps = torch.ones(num_seqs, dtype=torch.float32, device=self.device)
+            self.model.lm_head.sample(hidden, temps, self.sampler.seed)
+        finally:
+            reset_context()
+
+    @torch.inference_mode()
+    def _profile_decode(self, bs: int) -> None:
+        set_context(False, slot_mapping=torch.zeros(bs, dtype=torch.int32, device=self.device),
+                    context_lens=torch.ones(bs, dtype=torch.int32, device=self.device),
+                    block_tables=torch.zeros(bs, self.max_blocks_per_seq, dtype=torch.int32, device=self.device))
+        try:
+            K.WORKSPACE.reserve(self._decode_workspace_bytes(bs), self.device)
+            hidden = self.model(torch.zeros(bs, dtype=torch.int64, device=self.device),
+                                torch.zeros(bs, dtype=torch.int64, device=self.device))
+            self.model.lm_head.sample(hidden, torch.ones(bs, dtype=torch.float32, device=self.device),
+                                      self.sampler.seed)
+        finally:
+            reset_context()
+
+    def _decode_workspace_bytes(self, bs: int) -> int:
+        cfg = self.config.hf_config
+        hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        return K.decode_workspace_bytes(bs, cfg.num_attention_heads // self.world_size,
+                                        cfg.num_key_value_heads // self.world_size, hd, self.max_blocks_per_seq,
+                                        self.block_size)
+
+    def allocate_kv_cache(self) -> None:
+        self.cache = CachePool(self.model, self.config, self.world_size)
+
+        def peak(fn) -> int:
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats()
+            base = torch.cuda.memory_allocated()
+            fn()
+            torch.cuda.synchronize()
+            return torch.cuda.max_memory_allocated() - base
+
+        prefill_peak = peak(self._profile_prefill)
+        self.cache.allocate(num_blocks=2)
+        decode_peak = peak(lambda: self._profile_decode(self._max_graph_bs()))
+        reserve = (0 if self.enforce_eager else decode_peak) + max(prefill_peak, decode_peak)
+        if self.config.num_kvcache_blocks > 0:
+            layout = self.cache.allocate(num_blocks=self.config.num_kvcache_blocks)
+        else:
+            layout = self.cache.allocate(reserve=reserve)
+        self.config.num_kvcache_blocks = layout.num_blocks
+
+    # ------------------------------------------------------------ step
+    def _decode_forward(self, bs: int) -> None:
+        d = self.decode_buffers.d
+        hidden = self.model(d["input_ids"][:bs], d["positions"][:bs])
+        self.sampler.seed.add_(1)
+        self.model.lm_head.sample(hidden, d["temperatures"][:bs], self.sampler.seed,
+                                  out=self.decode_buffers.sampled[:bs])
+
+    @torch.inference_mode()
+    def capture_cudagraph(self) -> None:
+        max_bs = self._max_graph_bs()
+        self.decode_buffers = DecodeBuffers(max_bs, self.max_blocks_per_seq, self.device)
+        K.WORKSPACE.reserve(self._decode_workspace_bytes(max_bs), self.device)
+        self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
+        if self.graph_bs[-1] != max_bs:
+            self.graph_bs.append(max_bs)
+        d = self.decode_buffers.d
+        seed0 = self.sampler.seed.clone()
+        self.graph_launches: dict[int, int] = {}
+        for bs in reversed(self.graph_bs):
+            set_context(False, slot_mapping=d["slot_mapping"][:bs], context_lens=d["context_lens"][:bs],
+                        block_tables=d["block_tables"][:bs])
+            self._decode_forward(bs)  # warm-up outside the graph
+            graph = torch.cuda.CUDAGraph()
+            calls0 = _lib.launch_count()
+            with torch.cuda.graph(graph, self.graph_pool):
+                self._decode_forward(bs)
+            self.graph_launches[bs] = _lib.launch_count() - calls0
+            if self.graph_pool is None:
+                self.graph_pool = graph.pool()
+            self.graphs[bs] = graph
+            torch.cuda.synchronize()
+            reset_context()
+        self.sampler.seed.copy_(seed0)
+
+    def _ensure_decode_buffers(self) -> None:
+        if not hasattr(self, "decode_buffers"):
+            self.decode_buffers = DecodeBuffers(self._max_graph_bs(), self.max_blocks_per_seq, self.device)
+
+    @torch.inference_mode()
+    def run(self, seqs: list[Sequence], is_prefill: bool) -> list[int]:
+        temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
+        if is_prefill:
+            meta = prefill_metadata(seqs, self.block_size)
+            arrays = [meta["input_ids"], meta["positions"], meta["cu_seqlens_q"], meta["cu_seqlens_k"],
+                      meta["slot_mapping"], temps]
+            if meta["block_tables"] is not None:
+                arrays.append(meta["block_tables"])
+            dev = self.staging.upload(arrays)
+            ids, pos, cu_q, cu_k, slots, t_dev = dev[:6]
+            set_context(True, cu_q, cu_k, meta["max_seqlen_q"], meta["max_seqlen_k"], slots, None,
+                        dev[6] if len(dev) > 6 else None)
+            try:
+                hidden = self.model(ids, pos)
+                self.sampler.seed.add_(1)
+                tokens = self.model.lm_head.sample(hidden, t_dev, self.sampler.seed)
+            finally:
+                reset_context()
+            return tokens.tolist()
+        meta = decode_metadata(seqs, self.block_size)
+        bs = len(seqs)
+        self._ensure_decode_buffers()
+        buf = self.decode_buffers
+        if bs > buf.max_bs or meta["block_tables"].shape[1] > buf.max_blocks:
+            raise RuntimeError(f"decode batch {bs} x {meta['block_tables'].shape[1]} blocks exceeds the "
+                               f"runner's {buf.max_bs} x {buf.max_blocks}")
+        bucket = next((b for b in getattr(self, "graph_bs", []) if b >= bs), bs)
+        buf.fill(meta, temps, bucket)
+        graph = self.graphs.get(bucket)
+        if graph is not None:
+            graph.replay()
+        else:
+            d = buf.d
+            set_context(False, slot_mapping=d["slot_mapping"][:bs], context_lens=d["context_lens"][:bs],
+                        block_tables=d["block_tables"][:bs])
+            try:
+                self._decode_forward(bs)
+            finally:
+                reset_context()
+        return buf.sampled[:bs].tolist()

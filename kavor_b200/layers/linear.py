@@ -1,0 +1,136 @@
+"""Tensor-parallel linear layers (drop-in for kavor/layers/linear.py).
+
+Sharding and checkpoint loaders follow linear.py:8-160: column-parallel layers
+split the output rows across ranks (QKV rows ordered [q | k | v] per rank,
+gate/up rows [gate | up] per rank), row-parallel layers split the input
+columns and all-reduce the partial products (bias added on rank 0 only).
+All projections go through ``linear()``, the single GEMM entry point of the
+package.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+
+def divide(numerator: int, denominator: int) -> int:
+    if numerator % denominator:
+        raise ValueError(f"{numerator} is not divisible by {denominator}")
+    return numerator // denominator
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x W^T (+ b) in bf16 with fp32 accumulation (cuBLAS through torch)."""
+    return F.linear(x, weight, bias)
+
+
+def _tp() -> tuple[int, int]:
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+class LinearBase(nn.Module):
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False, tp_dim: int | None = None):
+        super().__init__()
+        self.tp_dim = tp_dim
+        self.tp_rank, self.tp_size = _tp()
+        self.weight = nn.Parameter(torch.empty(output_size, input_size))
+        self.weight.weight_loader = self.weight_loader
+        if bias:
+            self.bias = nn.Parameter(torch.empty(output_size))
+            self.bias.weight_loader = self.weight_loader
+        else:
+            self.register_parameter("bias", None)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor, *args):
+        raise NotImplementedError
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        raise NotImplementedError
+
+
+class ReplicatedLinear(LinearBase):
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False):
+        super().__init__(input_size, output_size, bias)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor):
+        param.data.copy_(loaded_weight)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return linear(x, self.weight, self.bias)
+
+
+class ColumnParallelLinear(LinearBase):
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False):
+        _, tp_size = _tp()
+        super().__init__(input_size, divide(output_size, tp_size), bias, 0)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor):
+        shard = param.data.size(self.tp_dim)
+        param.data.copy_(loaded_weight.narrow(self.tp_dim, self.tp_rank * shard, shard))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return linear(x, self.weight, self.bias)
+
+
+class MergedColumnParallelLinear(ColumnParallelLinear):
+
+    def __init__(self, input_size: int, output_sizes: list[int], bias: bool = False):
+        self.output_sizes = output_sizes
+        super().__init__(input_size, sum(output_sizes), bias)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor, loaded_shard_id: int):
+        offset = sum(self.output_sizes[:loaded_shard_id]) // self.tp_size
+        size = self.output_sizes[loaded_shard_id] // self.tp_size
+        dst = param.data.narrow(self.tp_dim, offset, size)
+        dst.copy_(loaded_weight.chunk(self.tp_size, self.tp_dim)[self.tp_rank])
+
+
+class QKVParallelLinear(ColumnParallelLinear):
+
+    def __init__(self, output_size: int, hidden_size: int, head_size: int, total_num_heads: int,
+                 total_num_kv_heads: int | None = None, q_gate: bool = False, bias: bool = False):
+        _, tp_size = _tp()
+        self.q_mult = 2 if q_gate else 1
+        total_num_kv_heads = total_num_kv_heads or total_num_heads
+        self.head_size = head_size
+        self.num_heads = divide(total_num_heads, tp_size)
+        self.num_kv_heads = divide(total_num_kv_heads, tp_size)
+        super().__init__(hidden_size, output_size, bias)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor, loaded_shard_id: str):
+        if loaded_shard_id not in ("q", "k", "v"):
+            raise ValueError(f"unknown qkv shard {loaded_shard_id!r}")
+        q_size = self.q_mult * self.num_heads * self.head_size
+        kv_size = self.num_kv_heads * self.head_size
+        offset, size = {"q": (0, q_size), "k": (q_size, kv_size), "v": (q_size + kv_size, kv_size)}[loaded_shard_id]
+        dst = param.data.narrow(self.tp_dim, offset, size)
+        dst.copy_(loaded_weight.chunk(self.tp_size, self.tp_dim)[self.tp_rank])
+
+
+class RowParallelLinear(LinearBase):
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False):
+        _, tp_size = _tp()
+        super().__init__(divide(input_size, tp_size), output_size, bias, 1)
+
+    def weight_loader(self, param: nn.Parameter, loaded_weight: torch.Tensor):
+        if param.data.ndim == 1:
+            param.data.copy_(loaded_weight)
+            return
+        shard = param.data.size(self.tp_dim)
+        param.data.copy_(loaded_weight.narrow(self.tp_dim, self.tp_rank * shard, shard))
+
+    def forward(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """``reduce=False`` returns the rank-local partial sum so the caller can
+        fuse the all-reduce with what follows."""
+        y = linear(x, self.weight, self.bias if self.tp_rank == 0 else None)
+        if reduce and self.tp_size > 1:
+            dist.all_reduce(y)
+        return y

@@ -1,0 +1,172 @@
+"""Qwen3 dense model on the kavor_b200 layers (drop-in for kavor/models/qwen3.py).
+
+Module tree, parameter names and the packed checkpoint mapping are those of
+qwen3.py:14-219, so reference checkpoints load unchanged. The forward is the
+same computation with the per-layer work fused into fewer kernels:
+
+* attention prologue (qwen3.py:80-89 + flash_attention_kvcache.py:72): after
+  the QKV GEMM, ONE kernel does q_norm, k_norm, RoPE on q and k and writes the
+  k/v rows into the paged cache, in place on the packed qkv rows;
+* attention: paged decode / varlen prefill kernels;
+* residual wiring (qwen3.py:149-162) with fused add+RMSNorm after every
+  row-parallel projection.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from kavor_b200 import _kernels as K
+from kavor_b200.layers.activation import SiluAndMul
+from kavor_b200.layers.attention import Attention
+from kavor_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
+from kavor_b200.layers.layernorm import RMSNorm
+from kavor_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp
+from kavor_b200.layers.rotary_embedding import get_rope
+from kavor_b200.utils.context import get_context
+
+
+def rope_theta_of(config, default: float = 1000000.0) -> float:
+    """rope theta from either the flat field or the rope_scaling/rope_parameters dict
+    (qwen3.py:57-58, :138-139)."""
+    theta = getattr(config, "rope_theta", None)
+    for name in ("rope_scaling", "rope_parameters"):
+        d = getattr(config, name, None)
+        if isinstance(d, dict) and "rope_theta" in d:
+            theta = d["rope_theta"]
+    return float(theta if theta is not None else default)
+
+
+class Qwen3Attention(nn.Module):
+
+    def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, max_position: int = 4096 * 32,
+                 head_dim: int | None = None, rms_norm_eps: float = 1e-06, qkv_bias: bool = False,
+                 rope_theta: float = 10000, rope_scaling: dict | None = None) -> None:
+        super().__init__()
+        _, tp_size = _tp()
+        if num_heads % tp_size or num_kv_heads % tp_size:
+            raise ValueError("attention heads must be divisible by the tensor-parallel size")
+        self.total_num_heads = num_heads
+        self.num_heads = num_heads // tp_size
+        self.total_num_kv_heads = num_kv_heads
+        self.num_kv_heads = num_kv_heads // tp_size
+        self.head_dim = head_dim or hidden_size // num_heads
+        self.q_size = self.num_heads * self.head_dim
+        self.kv_size = self.num_kv_heads * self.head_dim
+        self.scaling = self.head_dim ** -0.5
+        self.qkv_bias = qkv_bias
+        self.rms_norm_eps = rms_norm_eps
+        self.qkv_proj = QKVParallelLinear((num_heads + 2 * num_kv_heads) * self.head_dim, hidden_size,
+                                          self.head_dim, num_heads, num_kv_heads, bias=qkv_bias)
+        self.o_proj = RowParallelLinear(num_heads * self.head_dim, hidden_size, bias=False)
+        if isinstance(rope_scaling, dict):
+            rope_theta = rope_scaling.get("rope_theta", rope_theta)
+        self.rotary_emb = get_rope(self.head_dim, rotary_dim=self.head_dim, max_position=max_position,
+                                   base=rope_theta)
+        self.attn = Attention(self.num_heads, self.head_dim, self.scaling, self.num_kv_heads)
+        if not qkv_bias:
+            self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
+            self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
+
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        qkv = self.qkv_proj(hidden_states)
+        ctx = get_context()
+        k_cache, v_cache = self.attn.k_cache[0], self.attn.v_cache[0]
+        has_cache = k_cache.numel() > 0
+        K.qknorm_rope_store(
+            qkv, self.num_heads, self.num_kv_heads, self.head_dim,
+            None if self.qkv_bias else self.q_norm.weight, None if self.qkv_bias else self.k_norm.weight,
+            self.rms_norm_eps, positions, self.rotary_emb.cos_sin_cache, self.rotary_emb.interleaved,
+            k_cache if has_cache else None, v_cache if has_cache else None,
+            ctx.slot_mapping if has_cache else None)
+        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+        q = q.view(-1, self.num_heads, self.head_dim)
+        k = k.view(-1, self.num_kv_heads, self.head_dim)
+        v = v.view(-1, self.num_kv_heads, self.head_dim)
+        o = self.attn(q, k, v, kv_stored=True)
+        return self.o_proj(o.flatten(1, -1), reduce=reduce)
+
+
+class Qwen3MLP(nn.Module):
+
+    def __init__(self, hidden_size: int, intermediate_size: int, hidden_act: str) -> None:
+        super().__init__()
+        if hidden_act != "silu":
+            raise ValueError(f"unsupported activation {hidden_act!r}")
+        self.gate_up_proj = MergedColumnParallelLinear(hidden_size, [intermediate_size] * 2, bias=False)
+        self.down_proj = RowParallelLinear(intermediate_size, hidden_size, bias=False)
+        self.act_fn = SiluAndMul()
+
+    def forward(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce)
+
+
+class Qwen3DecoderLayer(nn.Module):
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.self_attn = Qwen3Attention(
+            hidden_size=config.hidden_size,
+            num_heads=config.num_attention_heads,
+            num_kv_heads=config.num_key_value_heads,
+            max_position=config.max_position_embeddings,
+            rms_norm_eps=config.rms_norm_eps,
+            qkv_bias=getattr(config, "attention_bias", True),
+            head_dim=getattr(config, "head_dim", None),
+            rope_theta=rope_theta_of(config),
+            rope_scaling=None,
+        )
+        self.mlp = Qwen3MLP(config.hidden_size, config.intermediate_size, config.hidden_act)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor,
+                residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+        if residual is None:
+            hidden_states, residual = self.input_layernorm(hidden_states), hidden_states
+        else:
+            hidden_states, residual = self.input_layernorm(hidden_states, residual)
+        hidden_states = self.self_attn(positions, hidden_states)
+        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
+        hidden_states = self.mlp(hidden_states)
+        return hidden_states, residual
+
+
+class Qwen3Model(nn.Module):
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.embed_tokens = VocabParallelEmbedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList([Qwen3DecoderLayer(config) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        hidden_states = self.embed_tokens(input_ids)
+        residual = None
+        for layer in self.layers:
+            hidden_states, residual = layer(positions, hidden_states, residual)
+        hidden_states, _ = self.norm(hidden_states, residual)
+        return hidden_states
+
+
+class Qwen3ForCausalLM(nn.Module):
+    packed_modules_mapping = {
+        "q_proj": ("qkv_proj", "q"),
+        "k_proj": ("qkv_proj", "k"),
+        "v_proj": ("qkv_proj", "v"),
+        "gate_proj": ("gate_up_proj", 0),
+        "up_proj": ("gate_up_proj", 1),
+    }
+
+    def __init__(self, config) -> None:
+        super().__init__()
+        self.model = Qwen3Model(config)
+        self.lm_head = ParallelLMHead(config.vocab_size, config.hidden_size)
+        if getattr(config, "tie_word_embeddings", False):
+            self.lm_head.weight.data = self.model.embed_tokens.weight.data
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        return self.model(input_ids, positions)
+
+    def compute_logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        return self.lm_head(hidden_states)

@@ -1,0 +1,146 @@
+"""Seeded inputs shared by the golden-fixture generator and the tests.
+
+Every case is rebuilt from its seed on demand (CPU generators are
+deterministic for a given torch build), so the committed fixtures only hold
+outputs and small metadata. Shapes follow BASELINE configs 1 and 3:
+Qwen3-0.6B / Qwen3-8B layer shapes, head_dim 128, block_size 256, context
+lengths U[100, 1024] from seed 0, KV pages N(0, 1), block tables a random
+permutation of the pool's blocks.
+"""
+from __future__ import annotations
+
+import random
+
+import torch
+
+QWEN3_06B = dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28, num_attention_heads=16,
+                 num_key_value_heads=8, head_dim=128, tie_word_embeddings=True)
+QWEN3_8B = dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36, num_attention_heads=32,
+                num_key_value_heads=8, head_dim=128, tie_word_embeddings=False)
+TINY = dict(hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=4,
+            num_key_value_heads=2, head_dim=128, tie_word_embeddings=False, vocab_size=4096)
+
+
+def hf_config(shape: dict, **over):
+    from transformers import Qwen3Config
+
+    kw = dict(vocab_size=151936, max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1e6,
+              attention_bias=False, hidden_act="silu")
+    kw.update(shape)
+    kw.update(over)
+    cfg = Qwen3Config(**kw)
+    cfg.rope_scaling = {"rope_theta": 1e6, "rope_type": "default"}
+    return cfg
+
+
+def checkpoint(shape: dict, seed: int = 0, layers: int | None = None) -> dict[str, torch.Tensor]:
+    """Full (TP=1) checkpoint tensors drawn on the CPU by kavor_b200's dummy loader."""
+    from kavor_b200.models import synthetic_checkpoint
+
+    over = {} if layers is None else {"num_hidden_layers": layers}
+    return dict(synthetic_checkpoint(hf_config(shape, **over), seed, torch.device("cpu")))
+
+
+def paged_pool(num_blocks: int, block_size: int, hkv: int, hd: int, seed: int):
+    """K/V caches in the reference page layout (K block then V block per page),
+    filled with N(0, 1) bf16. Returns (pool, k_cache, v_cache)."""
+    g = torch.Generator().manual_seed(seed)
+    pool = torch.randn(num_blocks, 2, block_size, hkv, hd, generator=g).to(torch.bfloat16)
+    return pool, pool[:, 0], pool[:, 1]
+
+
+def decode_batch(batch: int, lo: int, hi: int, block_size: int, seed: int, spare_blocks: int = 4):
+    """Context lengths U[lo, hi] (random.Random(seed)), block tables from a
+    permutation of the pool (torch generator seed + 1). Returns
+    (context_lens, block_tables [-1 padded], num_blocks, positions, slot_mapping)."""
+    rng = random.Random(seed)
+    ctx = [rng.randint(lo, hi) for _ in range(batch)]
+    need = [(c + block_size - 1) // block_size for c in ctx]
+    num_blocks = sum(need) + spare_blocks
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(seed + 1)).tolist()
+    width = max(need)
+    tables, k = [], 0
+    for n in need:
+        tables.append(perm[k:k + n] + [-1] * (width - n))
+        k += n
+    positions = [c - 1 for c in ctx]
+    slots = [tables[i][(c - 1) // block_size] * block_size + (c - 1) % block_size for i, c in enumerate(ctx)]
+    return (torch.tensor(ctx, dtype=torch.int32), torch.tensor(tables, dtype=torch.int32), num_blocks,
+            torch.tensor(positions, dtype=torch.int64), torch.tensor(slots, dtype=torch.int32))
+
+
+def config1_layer_case(seed: int = 0) -> dict:
+    """one Qwen3-0.6B decoder layer, one decode step, B = 16."""
+    shape = QWEN3_06B
+    hd, hkv = shape["head_dim"], shape["num_key_value_heads"]
+    ctx, tables, nblk, pos, slots = decode_batch(16, 100, 1024, 256, seed)
+    pool, k_cache, v_cache = paged_pool(nblk, 256, hkv, hd, seed + 2)
+    g = torch.Generator().manual_seed(seed + 3)
+    hidden = torch.randn(16, shape["hidden_size"], generator=g).to(torch.bfloat16)
+    residual = torch.randn(16, shape["hidden_size"], generator=g).to(torch.bfloat16)
+    ckpt = checkpoint(shape, seed, layers=1)
+    layer = {k[len("model.layers.0."):]: v for k, v in ckpt.items() if k.startswith("model.layers.0.")}
+    return dict(shape=shape, layer=layer, hidden=hidden, residual=residual, pool=pool, k_cache=k_cache,
+                v_cache=v_cache, context_lens=ctx, block_tables=tables, positions=pos, slot_mapping=slots)
+
+
+def host_workload():
+    """Scripted request stream for the scheduler / metadata trace (block_size 4):
+    shared prefixes, a prompt longer than the token budget (chunked prefill),
+    a pool small enough to force preemption, and an eos stop."""
+    base = [(7 * i + 3) % 89 + 1 for i in range(40)]
+    prompts = [
+        base[:30],                                # 0
+        base[:16] + [5, 6, 7, 8, 9, 10, 11, 12],  # 1: 4 cached blocks once 0 is hashed
+        [2, 4, 6, 8, 10, 12, 14],                 # 2
+        [(3 * i) % 50 + 1 for i in range(70)],    # 3: longer than the 64-token budget
+        [(3 * i) % 50 + 1 for i in range(70)],    # 4: identical to 3 (prefix hit on 17 blocks)
+        base[:30],                                # 5: identical to 0
+    ]
+    params = [(12, False), (9, False), (20, False), (6, True), (7, True), (5, False)]
+    arrivals = {0: [0, 1, 2], 3: [3], 6: [4, 5]}  # step -> request indices added before it
+    config = dict(max_num_seqs=4, max_num_batched_tokens=64, eos=0, kvcache_block_size=4, num_kvcache_blocks=28)
+    return prompts, params, arrivals, config
+
+
+def host_token(req: int, step: int, length: int) -> int:
+    """Deterministic 'sampled' token; request 2 emits eos (0) as its 4th completion token."""
+    return (req * 31 + step * 7 + length) % 97 + 1
+
+
+def _plain(v):
+    if v is None or isinstance(v, (int, float, bool)):
+        return v
+    if hasattr(v, "tolist"):
+        return v.tolist()
+    return list(v)
+
+
+def run_host_trace(make_seq, scheduler, meta_prefill, meta_decode, max_steps: int = 1000):
+    """Drive ``scheduler`` through host_workload(); returns (per-step trace, completions).
+
+    Each trace entry holds the scheduled request indices, the prefill flag,
+    the metadata the model runner would upload (plain lists) and the tokens
+    fed back to postprocess."""
+    prompts, params, arrivals, _ = host_workload()
+    seqs: dict[int, object] = {}
+    trace = []
+    last_arrival = max(arrivals)
+    for step in range(max_steps):
+        for r in arrivals.get(step, []):
+            seqs[r] = make_seq(prompts[r], params[r])
+            scheduler.add(seqs[r])
+        if scheduler.is_finished():
+            if step > last_arrival:
+                break
+            continue
+        sched, is_prefill = scheduler.schedule()
+        ids = {id(s): r for r, s in seqs.items()}
+        reqs = [ids[id(s)] for s in sched]
+        meta = meta_prefill(sched) if is_prefill else meta_decode(sched)
+        tokens = [0 if (r == 2 and s.num_completion_tokens == 3) else host_token(r, step, len(s))
+                  for r, s in zip(reqs, sched)]
+        scheduler.postprocess(sched, tokens, is_prefill)
+        trace.append({"step": step, "prefill": bool(is_prefill), "reqs": reqs, "tokens": tokens,
+                      "meta": {k: _plain(v) for k, v in meta.items()}})
+    return trace, {r: list(s.completion_token_ids) for r, s in seqs.items()}

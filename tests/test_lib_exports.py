@@ -1,0 +1,69 @@
+"""The C-ABI library builds, loads and exports exactly the entry points that
+include/kavor_b200.h declares (no GPU needed: only host-side argument checks
+are exercised, nothing is launched)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from kavor_b200 import _lib, build
+
+    build.build()
+    return _lib.load()
+
+
+def _declared():
+    text = (ROOT / "include" / "kavor_b200.h").read_text()
+    return set(re.findall(r"^(?:int|const char\*)\s+(kvb_\w+)\(", text, flags=re.M))
+
+
+def test_header_and_binding_agree():
+    from kavor_b200 import _lib
+
+    assert _declared() == set(_lib.exported_symbols())
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in _declared():
+        assert hasattr(lib, name), name
+
+
+def test_only_the_api_is_exported(lib):
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(ROOT / "kavor_b200" / "libkavor_b200.so")],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == _declared()
+
+
+def test_version_and_host_side_validation(lib):
+    assert lib.kvb_version() == 100
+    # invalid sizes are rejected on the host with a negative status and a message
+    rc = lib.kvb_store_kv(None, 0, None, 0, None, None, 0, 0, 256, 8, 128, None, -1, None)
+    assert rc < 0
+    assert b"kvb_store_kv" in lib.kvb_last_error()
+    rc = lib.kvb_paged_decode_attn(None, 0, 0, None, None, 10, 0, 256, None, 0, 4, None, None, 0, 0,
+                                   4, 32, 8, 64, 0.1, 0, None, 0, None)
+    assert rc < 0 and b"head_dim" in lib.kvb_last_error()
+    n = ctypes.c_size_t(123)
+    assert lib.kvb_paged_decode_attn_workspace_size(256, 32, 8, 128, 5, 256, 1, ctypes.byref(n)) == 0
+    assert n.value == 0  # a single split needs no scratch
+    assert lib.kvb_paged_decode_attn_workspace_size(1, 32, 8, 128, 5, 256, 4, ctypes.byref(n)) == 0
+    assert n.value == 1 * 32 * 4 * (128 + 1) * 4
+
+
+def test_ops_raise_without_a_cuda_tensor():
+    import torch
+
+    from kavor_b200 import _kernels as K
+
+    x = torch.zeros(4, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.rmsnorm(x, torch.ones(128, dtype=torch.bfloat16), 1e-6)

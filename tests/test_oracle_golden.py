@@ -1,0 +1,114 @@
+"""Pin the CPU oracle to the reference: every restated op is checked against
+fixtures produced by the reference's own code (tests/golden/make_golden.py)."""
+import torch
+
+import cases
+from conftest import GOLDEN
+from oracle import model as omodel
+from oracle import ops
+
+EPS = 1e-6
+
+
+def _load(name):
+    return torch.load(GOLDEN / name, weights_only=False)
+
+
+def test_rmsnorm_matches_reference_eager():
+    g = _load("ops_golden.pt")
+    for name in ("rms_2d", "rms_4096", "rms_qk"):
+        case = g[name]
+        assert torch.equal(ops.rmsnorm(case["x"], case["w"], EPS), case["y"]), name
+
+
+def test_add_rmsnorm_matches_reference_eager():
+    case = _load("ops_golden.pt")["add_rms"]
+    y, r = ops.add_rmsnorm(case["x"], case["r"], case["w"], EPS)
+    assert torch.equal(r, case["r_out"])
+    assert torch.equal(y, case["y"])
+
+
+def test_rope_cache_and_rotation_match_reference():
+    g = _load("ops_golden.pt")
+    rc = g["rope_cache"]
+    cache = ops.cos_sin_cache(128, rc["max_position"], 1e6)
+    assert torch.equal(cache[rc["rows"]], rc["values"])
+    case = g["rope"]
+    T, Hq, Hkv = 12, 8, 2
+    q = case["qkv"][:, :Hq * 128].view(T, Hq, 128)
+    k = case["qkv"][:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
+    assert torch.equal(ops.rope(q, case["pos"], cache), case["q"])
+    assert torch.equal(ops.rope(k, case["pos"], cache), case["k"])
+    assert torch.equal(ops.rope(q, case["pos"], cache, interleaved=True), case["q_il"])
+    assert torch.equal(ops.rope(k, case["pos"], cache, interleaved=True), case["k_il"])
+
+
+def test_product_rope_table_is_the_reference_table():
+    from kavor_b200.layers.rotary_embedding import build_cos_sin_cache
+
+    rc = _load("ops_golden.pt")["rope_cache"]
+    assert torch.equal(build_cos_sin_cache(128, rc["max_position"], 1e6)[rc["rows"]], rc["values"])
+
+
+def test_silu_mul_within_one_rounding_of_reference_eager():
+    # the reference eager path rounds silu(g) to bf16 before the product, the
+    # compiled path (and the oracle) round once: allow one bf16 ulp
+    case = _load("ops_golden.pt")["silu"]
+    y = ops.silu_mul(case["x"])
+    torch.testing.assert_close(y.float(), case["y"].float(), rtol=2 ** -7, atol=1e-6)
+
+
+def _oracle_layer(case, residual):
+    shape = omodel.Shape(hidden=1024, inter=3072, layers=1, hq=16, hkv=8)
+    p = {"model.layers.0." + k: v for k, v in case["layer"].items()}
+    pool = case["pool"].clone()
+    batch = omodel.Batch(False, case["positions"], case["slot_mapping"], context_lens=case["context_lens"],
+                         block_tables=case["block_tables"])
+    cache = ops.cos_sin_cache(128, 40960, 1e6)
+    return omodel.decoder_layer(p, 0, case["hidden"].clone(), residual, batch, (pool[:, 0], pool[:, 1]), shape, cache)
+
+
+def test_decoder_layer_matches_reference_layer():
+    """one 0.6B decoder layer, one decode step, B=16."""
+    case = cases.config1_layer_case(0)
+    gold = _load("layer_golden.pt")
+    for variant, res in (("first", None), ("later", case["residual"].clone())):
+        h, r = _oracle_layer(case, res)
+        torch.testing.assert_close(r.float(), gold[variant]["residual"].float(), atol=2e-2, rtol=1e-2)
+        torch.testing.assert_close(h.float(), gold[variant]["hidden"].float(), atol=2e-2, rtol=1e-2)
+
+
+def test_tiny_model_greedy_matches_reference_model():
+    gold = _load("tiny_model_golden.pt")
+    shape = omodel.Shape(hidden=512, inter=1024, layers=2, hq=4, hkv=2, vocab=4096)
+    p = cases.checkpoint(cases.TINY, seed=5)
+    kv = [(torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16), torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16))
+          for _ in range(2)]
+    seqs = [list(x) for x in gold["prompts"]]
+    tables = gold["tables"]
+    ids = torch.tensor([t for s in seqs for t in s])
+    pos = torch.tensor([i for s in seqs for i in range(len(s))])
+    cu = torch.tensor([0] + list(torch.tensor([len(s) for s in seqs]).cumsum(0)), dtype=torch.int32)
+    slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))])
+    _, logits = omodel.forward(p, ids, omodel.Batch(True, pos, slots, cu, cu), kv, shape)
+    for step in gold["steps"]:
+        cos = torch.nn.functional.cosine_similarity(logits.float(), step["logits"].float(), dim=-1)
+        assert cos.min().item() > 0.999
+        tok = logits.float().argmax(-1).tolist()
+        assert tok == step["tokens"]
+        for b, t in enumerate(tok):
+            seqs[b].append(t)
+        ids = torch.tensor([s[-1] for s in seqs])
+        pos = torch.tensor([len(s) - 1 for s in seqs])
+        ctx = torch.tensor([len(s) for s in seqs], dtype=torch.int32)
+        slots = torch.tensor([tables[b][0] * 256 + len(s) - 1 for b, s in enumerate(seqs)])
+        batch = omodel.Batch(False, pos, slots, context_lens=ctx, block_tables=torch.tensor(tables, dtype=torch.int32))
+        _, logits = omodel.forward(p, ids, batch, kv, shape)
+
+
+def test_philox_known_answer():
+    """Philox4x32-10 known-answer vectors of the Random123 distribution
+    (kat_vectors: counter 0, key 0 and counter/key all-ones)."""
+    c = ops.philox4x32_10
+    # counter (0,0,0,0), key (0,0)
+    assert c([0], 0)[0].tolist() == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]

@@ -283,7 +283,7 @@ def run_ours(args) -> int:
     model_dir = write_model_dir(os.path.join(tmp, f"r{rank}"), args.model)
     cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world, max_model_len=max_len,
                  max_num_seqs=B, max_num_batched_tokens=4096, num_kvcache_blocks=B * blocks_per_seq + 8,
-                 rdzv_port=1)
+                 rdzv_port=1, graph_batch_sizes=(B,))
     runner = ModelRunner(cfg, rank, None)
     with torch.no_grad():
         runner.cache.pools.view(torch.bfloat16).normal_(0.0, 1.0)  # resident KV pages, N(0, 1)
@@ -314,10 +314,12 @@ def run_ours(args) -> int:
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("kvb_timed")
     start.record()
     for _ in range(args.steps):
         graph.replay()
     end.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     t_dev = max_over_ranks(start.elapsed_time(end) / 1e3)
@@ -353,10 +355,9 @@ def run_ours(args) -> int:
     peak, peak_src = measured_peaks()
     prof = ROOT / "profiles" / "decode_attention_traffic.json"
     traffic = None
-    if prof.exists():
-        tr = json.loads(prof.read_text())
-        key = f"{args.model}_B{B}_ctx{ctx0}_tp{world}"
-        traffic = tr.get(key)
+    if prof.exists():  # ncu DRAM bytes of a captured small case, scaled by the units of this launch
+        per_unit = json.loads(prof.read_text())["bytes_per_seq_kvhead_ctx1024"]
+        traffic = per_unit * B * hkv * ctx_now / 1024
     achieved = a_bytes / t_attn / 1e9
     roofline = {"kernel": "decode_attn_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,

@@ -45,7 +45,7 @@ const char* kvb_last_error(void);
 
 /* OR of the device-side error bits raised by kernels on the CURRENT device
  * since the last clear (1: block table, 2: slot, 4: wait timeout, 8: token id,
- * 16: peer wait timeout). Synchronises the device. Returns 0 or a CUDA error. */
+ * 16: peer (all-reduce flag) wait timeout). Synchronises the device. Returns 0 or a CUDA error. */
 int kvb_device_error(unsigned* bits, int clear);
 
 /* Number of SMs of the current device (used by the host-side heuristics). */
@@ -153,6 +153,56 @@ int kvb_prefill_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h, cons
                      const int32_t* cu_seqlens_k, int batch, int max_seqlen_q, void* out, int64_t out_stride_t,
                      int64_t out_stride_h, int num_q_heads, int num_kv_heads, int head_dim, float scale,
                      void* stream);
+
+/* --------------------------------------------------------------------- GEMM */
+
+/* Bytes of scratch kvb_gemm_bf16 needs for this shape (0 when it does not split
+ * K). splits = 0 means the heuristic the call itself would pick. */
+int kvb_gemm_workspace_size(int M, int N, int K, int splits, size_t* bytes);
+
+/* y[M, N] = x[M, K] * w[N, K]^T (F.linear of linear.py:50,73,157 and
+ * embed_head.py:61) on tcgen05 tensor cores: bf16 operands, fp32 accumulation
+ * in TMEM, bf16 result; rows of x, w, y with leading dimensions ldx, ldw, ldy
+ * (elements; x and w rows 16-byte aligned). The weight is streamed once per
+ * 256-token tile through TMA. When the heuristic splits K, fp32 partials go
+ * through `workspace` (256-byte aligned, >= kvb_gemm_workspace_size bytes, its
+ * first bytes are per-tile tickets that must be zero before the first call —
+ * every call leaves them zero again); results are deterministic. */
+int kvb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
+                  int splits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------- tensor-parallel all-reduce (NVLink) */
+
+/* Size in bytes of the CUDA IPC handle kvb_comm_create writes. */
+int kvb_comm_ipc_handle_size(void);
+
+/* Per-rank communicator of a TP group (one process per GPU, current device).
+ * Allocates this rank's symmetric area (flags, three partial-sum buffers of
+ * max_bytes each, a result area) and writes its CUDA IPC handle to ipc_handle.
+ * The caller gathers every rank's handle (rank order) over any channel and
+ * passes them to kvb_comm_open_peers. Replaces the NCCL all-reduces of
+ * linear.py:158-159 and embed_head.py:39-41 (NCCL stays for init/barriers). */
+int kvb_comm_create(int rank, int world, size_t max_bytes, void** comm, void* ipc_handle);
+int kvb_comm_open_peers(void* comm, const void* handles);
+/* Device pointer of partial-sum buffer `index` (0..2): the row-parallel GEMM /
+ * the embedding writes its rank-local [tokens, hidden] bf16 result there. */
+int kvb_comm_data_buffer(void* comm, int index, void** ptr, size_t* bytes);
+int kvb_comm_destroy(void* comm);
+
+/* Fused all-reduce + residual add + RMSNorm over the TP group
+ * (linear.py:156-160 followed by layernorm.py:114-140; with residual_in =
+ * NULL the embedding all-reduce followed by qwen3.py:155-156):
+ *   y = bf16(sum over ranks of buffer[data_index]) (fp32 sum in rank order),
+ *   r = fp32(y) + fp32(residual_in) (or y), residual_out <- bf16(r),
+ *   out = bf16(bf16(r * rsqrt(mean(r^2) + eps)) * weight).
+ * Every rank of the group must make the same calls in the same order. mode:
+ * 0 automatic, 1 one-shot (every rank reduces every row), 2 two-shot (each
+ * rank reduces 1/N of the rows, then exchanges results). Peer waits are
+ * bounded (~1 s); on expiry the kernel raises device error bit 16 and returns.
+ * residual_out may alias residual_in. Consecutive calls must use different
+ * data buffers. */
+int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void* residual_in, void* residual_out, void* out,
+                              const void* weight, int tokens, int hidden, float eps, int mode, void* stream);
 
 /* ------------------------------------------------------------------ sampler */
 

@@ -60,6 +60,23 @@ class _Workspace:
 WORKSPACE = _Workspace()
 
 
+class _ZeroedWorkspace(_Workspace):
+    """Like _Workspace but zero-filled at allocation (the GEMM's split-K tickets
+    must start at zero; every GEMM call leaves them at zero)."""
+
+    def reserve(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        cur = self.buf.get(idx)
+        if cur is not None and cur.numel() >= nbytes:
+            return cur
+        new = super().reserve(nbytes, device)
+        new.zero_()
+        return new
+
+
+GEMM_WORKSPACE = _ZeroedWorkspace()
+
+
 # ------------------------------------------------------------------ KV cache
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   slot_mapping: torch.Tensor) -> None:
@@ -253,6 +270,31 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
                   k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), 0, 0, 0, None, 0, 0,
                   cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, int(max_seqlen_q), out.data_ptr(),
                   out.stride(0), out.stride(1), Hq, Hkv, hd, float(scale), _stream())
+    return out
+
+
+# ------------------------------------------------------------------ GEMM
+def gemm_workspace_bytes(M: int, N: int, K: int, splits: int = 0) -> int:
+    n = ctypes.c_size_t(0)
+    _lib.call("kvb_gemm_workspace_size", M, N, K, splits, ctypes.byref(n))
+    return int(n.value)
+
+
+def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
+    """y = x @ weight^T on tcgen05 tensor cores (bf16 in/out, fp32 accumulate)."""
+    _cuda(x, "x", _BF16)
+    _cuda(weight, "weight", _BF16)
+    _req(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1], "gemm: x [M, K], weight [N, K]")
+    _req(x.stride(1) == 1 and weight.stride(1) == 1, "gemm: rows must be contiguous")
+    M, K = x.shape
+    N = weight.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    need = gemm_workspace_bytes(M, N, K, splits)
+    ws = GEMM_WORKSPACE.reserve(need, x.device) if need else None
+    _lib.call("kvb_gemm_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
+              out.stride(0), M, N, K, splits, ws.data_ptr() if ws is not None else None,
+              ws.numel() if ws is not None else 0, _stream())
     return out
 
 

@@ -37,12 +37,22 @@ SIGNATURES: dict[str, list] = {
     "kvb_sample": [P, L, P, P, P, I, I, P],
     "kvb_sample_partial": [P, L, P, P, P, P, I, I, L, L, P],
     "kvb_sample_combine": [P, P, I, P, I, P],
+    "kvb_gemm_workspace_size": [I, I, I, I, POINTER(c_size_t)],
+    "kvb_gemm_bf16": [P, L, P, L, P, L, I, I, I, I, P, c_size_t, P],
+    "kvb_comm_ipc_handle_size": [],
+    "kvb_comm_create": [I, I, c_size_t, POINTER(c_void_p), P],
+    "kvb_comm_open_peers": [P, P],
+    "kvb_comm_data_buffer": [P, I, POINTER(c_void_p), POINTER(c_size_t)],
+    "kvb_comm_destroy": [P],
+    "kvb_allreduce_add_rmsnorm": [P, I, P, P, P, P, I, I, F, I, P],
 }
 
 _lib: ctypes.CDLL | None = None
 
 # Entry points that only query or report (everything else launches kernels).
-_QUERIES = {"kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size"}
+_QUERIES = {"kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
+            "kvb_gemm_workspace_size", "kvb_comm_ipc_handle_size", "kvb_comm_create", "kvb_comm_open_peers",
+            "kvb_comm_data_buffer", "kvb_comm_destroy"}
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.
 CALLS: dict[str, int] = {}
@@ -80,7 +90,10 @@ def check(status: int, name: str) -> None:
 
 def call(name: str, *args) -> None:
     """Call entry point ``name`` and raise on a non-zero status."""
-    check(getattr(load(), name)(*args), name)
+    rc = getattr(load(), name)(*args)
+    if name == "kvb_comm_ipc_handle_size":
+        return rc
+    check(rc, name)
     if name not in _QUERIES:
         CALLS[name] = CALLS.get(name, 0) + 1
 

@@ -2,8 +2,9 @@
 
 Extra fields over the reference: ``load_format`` ("auto" reads the checkpoint
 in ``model``, "dummy" draws a seeded random checkpoint of the same shapes),
-``seed`` for that draw, and ``enable_prefix_caching`` (the reference always
-caches prefixes).
+``seed`` for that draw, ``enable_prefix_caching`` (the reference always
+caches prefixes) and ``graph_batch_sizes`` (the decode batch buckets captured
+as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16).
 """
 from __future__ import annotations
 
@@ -48,6 +49,8 @@ class Config:
     load_format: str = "auto"
     seed: int = 0
     enable_prefix_caching: bool = True
+    graph_batch_sizes: tuple[int, ...] | None = None  # decode buckets to capture (None: 1,2,4,8,16,32,...)
+    fused_allreduce: bool = True  # TP > 1: NVLink all-reduce fused with add+RMSNorm (False: NCCL + separate norm)
 
     def __post_init__(self):
         if not os.path.isdir(self.model):

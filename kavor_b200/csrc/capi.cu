@@ -28,6 +28,8 @@ int read_device_error_elementwise(unsigned*, int);
 int read_device_error_decode(unsigned*, int);
 int read_device_error_prefill(unsigned*, int);
 int read_device_error_sampler(unsigned*, int);
+int read_device_error_gemm(unsigned*, int);
+int read_device_error_allreduce(unsigned*, int);
 
 }  // namespace kvb
 
@@ -41,7 +43,8 @@ extern "C" int kvb_device_error(unsigned* bits, int clear) {
   if (e != cudaSuccess) return kvb::cuda_status(e, "kvb_device_error: synchronize");
   unsigned acc = 0, w = 0;
   int (*readers[])(unsigned*, int) = {kvb::read_device_error_elementwise, kvb::read_device_error_decode,
-                                      kvb::read_device_error_prefill, kvb::read_device_error_sampler};
+                                      kvb::read_device_error_prefill, kvb::read_device_error_sampler,
+                                      kvb::read_device_error_gemm, kvb::read_device_error_allreduce};
   for (auto fn : readers) {
     int rc = fn(&w, clear);
     if (rc) return rc;

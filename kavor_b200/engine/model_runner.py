@@ -28,6 +28,7 @@ from kavor_b200 import _kernels as K
 from kavor_b200 import _lib
 from kavor_b200.engine.cache_pool import CachePool
 from kavor_b200.engine.sequence import Sequence
+from kavor_b200.layers.allreduce import TPAllReduce, set_tp_allreduce
 from kavor_b200.layers.sampler import Sampler
 from kavor_b200.models import AutoModelForCausalLM
 from kavor_b200.utils.context import reset_context, set_context
@@ -103,7 +104,7 @@ class Staging:
         self._grow(capacity)
 
     def _grow(self, nbytes: int) -> None:
-        self.host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        self.host = torch.empty(nbytes, dtype=torch.uint8, device="cpu", pin_memory=True)
         self.dev = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
 
     def upload(self, arrays: list[np.ndarray]) -> list[torch.Tensor]:
@@ -138,7 +139,7 @@ class DecodeBuffers:
         layout["block_tables"] = (off, np.int32, (max_bs, max_blocks))
         off += max_bs * max_blocks * 4
         self.nbytes = off
-        self.host = torch.zeros(off, dtype=torch.uint8, pin_memory=True)
+        self.host = torch.zeros(off, dtype=torch.uint8, device="cpu", pin_memory=True)
         self.dev = torch.zeros(off, dtype=torch.uint8, device=device)
         self.h, self.d = {}, {}
         hv = self.host.numpy()
@@ -194,6 +195,11 @@ class ModelRunner:
             Sequence.block_size = config.kvcache_block_size
             self.model = AutoModelForCausalLM.from_pretrained(config.hf_config, load_format=config.load_format,
                                                               seed=config.seed)
+            self.tp_allreduce = None
+            if self.world_size > 1 and config.fused_allreduce:
+                max_tokens = max(config.max_num_batched_tokens, self._max_graph_bs())
+                self.tp_allreduce = TPAllReduce(max_tokens, config.hf_config.hidden_size, self.device)
+                set_tp_allreduce(self.tp_allreduce)
             self.sampler = Sampler()
             self.staging = Staging(self.device)
             self.allocate_kv_cache()
@@ -271,6 +277,10 @@ class ModelRunner:
         self.graphs.clear()
         self.graph_pool = None
         torch.cuda.synchronize()
+        if self.tp_allreduce is not None:
+            set_tp_allreduce(None)
+            self.tp_allreduce.close()
+            self.tp_allreduce = None
         if self.owns_process_group and dist.is_initialized():
             dist.destroy_process_group()
 
@@ -353,10 +363,14 @@ class ModelRunner:
     def capture_cudagraph(self) -> None:
         max_bs = self._max_graph_bs()
         self.decode_buffers = DecodeBuffers(max_bs, self.max_blocks_per_seq, self.device)
-        K.WORKSPACE.reserve(self._decode_workspace_bytes(max_bs), self.device)
-        self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
-        if self.graph_bs[-1] != max_bs:
+        if self.config.graph_batch_sizes:
+            self.graph_bs = sorted(b for b in set(self.config.graph_batch_sizes) if 1 <= b <= max_bs)
+        else:
+            self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
+        if not self.graph_bs or self.graph_bs[-1] != max_bs:
             self.graph_bs.append(max_bs)
+        # scratch is allocated outside capture, sized for the largest need of any bucket
+        K.WORKSPACE.reserve(max(self._decode_workspace_bytes(b) for b in self.graph_bs), self.device)
         d = self.decode_buffers.d
         seed0 = self.sampler.seed.clone()
         self.graph_launches: dict[int, int] = {}

@@ -1,0 +1,101 @@
+"""Fused tensor-parallel all-reduce + residual add + RMSNorm over NVLink.
+
+Replaces, for TP > 1, the NCCL all-reduce after every row-parallel projection
+and the vocab-parallel embedding (linear.py:158-159, embed_head.py:39-41)
+together with the add+RMSNorm that always follows it in Qwen3
+(qwen3.py:155-160, 185). Each rank owns a symmetric area allocated by the
+library (``kvb_comm_create``); the CUDA IPC handles are exchanged once over
+the existing process group, after which every call is a single kernel that
+reads the peers' partial sums directly over NVLink.
+
+The producing kernel (row-parallel GEMM or embedding) writes its rank-local
+result straight into one of three data buffers of the symmetric area
+(``partial_buffer``); consecutive reductions must use different buffers, which
+``next_buffer`` guarantees within a forward (the embedding uses buffer 2,
+the layers alternate 0 and 1).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from kavor_b200 import _lib
+
+
+class _CudaArray:
+    """Zero-copy torch view of device memory owned by the library."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class TPAllReduce:
+
+    EMBED_BUFFER = 2
+
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device, group=None):
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.device = device
+        lib = _lib.load()
+        hs = lib.kvb_comm_ipc_handle_size()
+        handle = (ctypes.c_ubyte * hs)()
+        self.comm = ctypes.c_void_p()
+        _lib.call("kvb_comm_create", self.rank, self.world, max_tokens * hidden * 2, ctypes.byref(self.comm), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        blob = b"".join(handles)
+        _lib.call("kvb_comm_open_peers", self.comm, ctypes.c_char_p(blob))
+        self.buffers = []
+        for i in range(3):
+            ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+            _lib.call("kvb_comm_data_buffer", self.comm, i, ctypes.byref(ptr), ctypes.byref(nbytes))
+            raw = torch.as_tensor(_CudaArray(ptr.value, nbytes.value), device=device)
+            self.buffers.append(raw.view(torch.bfloat16).view(max_tokens, hidden))
+        dist.barrier(group=group)
+        self._next = 0
+
+    def start_forward(self) -> None:
+        self._next = 0
+
+    def next_buffer(self, tokens: int) -> tuple[int, torch.Tensor]:
+        idx = self._next
+        self._next ^= 1
+        return idx, self.partial_buffer(idx, tokens)
+
+    def partial_buffer(self, index: int, tokens: int) -> torch.Tensor:
+        if tokens > self.max_tokens:
+            raise RuntimeError(f"{tokens} tokens exceed the all-reduce buffers ({self.max_tokens})")
+        return self.buffers[index][:tokens]
+
+    def reduce_norm(self, index: int, tokens: int, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                    mode: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+        """(RMSNorm(sum + residual), sum + residual) with the residual updated in place."""
+        out = torch.empty(tokens, self.hidden, dtype=torch.bfloat16, device=self.device)
+        res_out = residual if residual is not None else torch.empty_like(out)
+        _lib.call("kvb_allreduce_add_rmsnorm", self.comm, index,
+                  residual.data_ptr() if residual is not None else None, res_out.data_ptr(), out.data_ptr(),
+                  weight.data_ptr(), tokens, self.hidden, float(eps), mode, torch.cuda.current_stream().cuda_stream)
+        return out, res_out
+
+    def close(self) -> None:
+        if self.comm:
+            _lib.call("kvb_comm_destroy", self.comm)
+            self.comm = ctypes.c_void_p()
+            self.buffers = []
+
+
+_TP: TPAllReduce | None = None
+
+
+def set_tp_allreduce(comm: TPAllReduce | None) -> None:
+    global _TP
+    _TP = comm
+
+
+def get_tp_allreduce() -> TPAllReduce | None:
+    return _TP

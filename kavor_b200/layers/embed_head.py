@@ -38,8 +38,8 @@ class VocabParallelEmbedding(nn.Module):
         shard = param.data.size(0)
         param.data.copy_(loaded_weight.narrow(0, self.tp_rank * shard, shard))
 
-    def forward(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        y = K.embedding(x, self.weight, self.vocab_start_idx, self.vocab_end_idx, self.num_embeddings)
+    def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        y = K.embedding(x, self.weight, self.vocab_start_idx, self.vocab_end_idx, self.num_embeddings, out=out)
         if reduce and self.tp_size > 1:
             dist.all_reduce(y)
         return y

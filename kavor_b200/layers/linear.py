@@ -21,9 +21,15 @@ def divide(numerator: int, denominator: int) -> int:
     return numerator // denominator
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x W^T (+ b) in bf16 with fp32 accumulation (cuBLAS through torch)."""
-    return F.linear(x, weight, bias)
+    if out is None:
+        return F.linear(x, weight, bias)
+    torch.matmul(x, weight.t(), out=out)
+    if bias is not None:
+        out.add_(bias)
+    return out
 
 
 def _tp() -> tuple[int, int]:
@@ -127,10 +133,10 @@ class RowParallelLinear(LinearBase):
         shard = param.data.size(self.tp_dim)
         param.data.copy_(loaded_weight.narrow(self.tp_dim, self.tp_rank * shard, shard))
 
-    def forward(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        """``reduce=False`` returns the rank-local partial sum so the caller can
-        fuse the all-reduce with what follows."""
-        y = linear(x, self.weight, self.bias if self.tp_rank == 0 else None)
+    def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``reduce=False`` returns the rank-local partial sum (written into
+        ``out`` when given) so the caller can fuse the all-reduce with what follows."""
+        y = linear(x, self.weight, self.bias if self.tp_rank == 0 else None, out=out)
         if reduce and self.tp_size > 1:
             dist.all_reduce(y)
         return y

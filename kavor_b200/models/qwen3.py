@@ -18,6 +18,7 @@ from torch import nn
 
 from kavor_b200 import _kernels as K
 from kavor_b200.layers.activation import SiluAndMul
+from kavor_b200.layers.allreduce import get_tp_allreduce
 from kavor_b200.layers.attention import Attention
 from kavor_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
 from kavor_b200.layers.layernorm import RMSNorm
@@ -68,7 +69,8 @@ class Qwen3Attention(nn.Module):
             self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
             self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
 
-    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor, reduce: bool = True,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         qkv = self.qkv_proj(hidden_states)
         ctx = get_context()
         k_cache, v_cache = self.attn.k_cache[0], self.attn.v_cache[0]
@@ -84,7 +86,7 @@ class Qwen3Attention(nn.Module):
         k = k.view(-1, self.num_kv_heads, self.head_dim)
         v = v.view(-1, self.num_kv_heads, self.head_dim)
         o = self.attn(q, k, v, kv_stored=True)
-        return self.o_proj(o.flatten(1, -1), reduce=reduce)
+        return self.o_proj(o.flatten(1, -1), reduce=reduce, out=out)
 
 
 class Qwen3MLP(nn.Module):
@@ -97,8 +99,8 @@ class Qwen3MLP(nn.Module):
         self.down_proj = RowParallelLinear(intermediate_size, hidden_size, bias=False)
         self.act_fn = SiluAndMul()
 
-    def forward(self, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
-        return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce)
+    def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce, out=out)
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -141,12 +143,36 @@ class Qwen3Model(nn.Module):
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        ar = get_tp_allreduce()
+        if ar is not None and self.embed_tokens.tp_size > 1:
+            return self._forward_fused_allreduce(ar, input_ids, positions)
         hidden_states = self.embed_tokens(input_ids)
         residual = None
         for layer in self.layers:
             hidden_states, residual = layer(positions, hidden_states, residual)
         hidden_states, _ = self.norm(hidden_states, residual)
         return hidden_states
+
+    def _forward_fused_allreduce(self, ar, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        """TP > 1: every all-reduce is fused with the add+RMSNorm after it; the
+        embedding and the row-parallel projections write their rank-local
+        partial sums straight into the communicator's NVLink-visible buffers."""
+        T = input_ids.numel()
+        ar.start_forward()
+        idx = ar.EMBED_BUFFER
+        self.embed_tokens(input_ids, reduce=False, out=ar.partial_buffer(idx, T))
+        residual = None
+        for layer in self.layers:
+            ln = layer.input_layernorm
+            x, residual = ar.reduce_norm(idx, T, residual, ln.weight, ln.eps)
+            idx, buf = ar.next_buffer(T)
+            layer.self_attn(positions, x, reduce=False, out=buf)
+            ln = layer.post_attention_layernorm
+            x, residual = ar.reduce_norm(idx, T, residual, ln.weight, ln.eps)
+            idx, buf = ar.next_buffer(T)
+            layer.mlp(x, reduce=False, out=buf)
+        out, _ = ar.reduce_norm(idx, T, residual, self.norm.weight, self.norm.eps)
+        return out
 
 
 class Qwen3ForCausalLM(nn.Module):

@@ -1,0 +1,141 @@
+"""Fused NVLink all-reduce + residual add + RMSNorm (kvb_allreduce_add_rmsnorm)
+on 2 GPUs, one process per GPU: parity with the oracle (sum of every rank's
+partial in rank order -> bf16 -> add+RMSNorm), one-shot and two-shot, with and
+without a residual, alternating buffers, CUDA-graph replay, and the bounded
+peer wait: a rank that skips a call makes the other rank's kernel give up after
+about a second and report device error bit 16 (no hang, no fault).
+NVLS is off for these processes (NCCL_NVLS_ENABLE=0) and the kernel uses plain
+peer loads/stores only."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+H = 4096
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _partial(rank, T, salt):
+    g = torch.Generator().manual_seed(1000 * salt + rank)
+    return torch.randn(T, H, generator=g).to(torch.bfloat16)
+
+
+def _expected(T, salt, residual, weight):
+    from oracle import ops
+
+    acc = sum(_partial(p, T, salt).float() for p in range(WORLD))  # rank order, fp32
+    y = acc.to(torch.bfloat16)
+    if residual is None:
+        return ops.rmsnorm(y, weight, 1e-6), y
+    return ops.add_rmsnorm(y, residual, weight, 1e-6)
+
+
+def _worker(rank, port, results):
+    import datetime
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch.distributed as dist
+
+    from kavor_b200 import _lib
+    from kavor_b200.layers.allreduce import TPAllReduce
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=WORLD, rank=rank, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    errors = []
+    try:
+        ar = TPAllReduce(2048, H, dev)
+        w = (torch.randn(H, generator=torch.Generator().manual_seed(5)) * 0.1 + 1).to(torch.bfloat16)
+        dw = w.to(dev)
+        salt, idx = 0, 0
+        for mode in (1, 2):
+            for T in (1, 7, 256, 1000):
+                for with_res in (False, True):
+                    salt += 1
+                    res = _partial(7, T, salt) if with_res else None
+                    ar.partial_buffer(idx, T).copy_(_partial(rank, T, salt).to(dev))
+                    dres = res.to(dev) if res is not None else None
+                    out, r = ar.reduce_norm(idx, T, dres, dw, 1e-6, mode=mode)
+                    idx ^= 1
+                    eo, er = _expected(T, salt, res, w)
+                    if not torch.equal(r.cpu(), er):
+                        errors.append(f"residual mode={mode} T={T} res={with_res}")
+                    if not torch.allclose(out.float().cpu(), eo.float(), atol=2e-2, rtol=2e-2):
+                        errors.append(f"out mode={mode} T={T} res={with_res}")
+        # CUDA graph: three chained reductions captured once, replayed with new data
+        T = 64
+        bufs = [ar.partial_buffer(i, T) for i in range(3)]
+        resid = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        g = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            o1, _ = ar.reduce_norm(2, T, resid, dw, 1e-6)
+            bufs[0].copy_(o1)
+            o2, _ = ar.reduce_norm(0, T, resid, dw, 1e-6)
+        for rep in range(3):
+            salt += 1
+            resid.zero_()
+            bufs[2].copy_(_partial(rank, T, salt).to(dev))
+            g.replay()
+            torch.cuda.synchronize()
+            e1, er1 = _expected(T, salt, torch.zeros(T, H, dtype=torch.bfloat16), w)
+            # second stage: every rank contributed its (identical) o1, plus residual er1
+            acc = (e1.float() * WORLD).to(torch.bfloat16)
+            from oracle import ops
+
+            e2, er2 = ops.add_rmsnorm(acc, er1, w, 1e-6)
+            if not torch.allclose(resid.float().cpu(), er2.float(), atol=2e-2, rtol=2e-2):
+                errors.append(f"graph replay {rep}: residual")
+            if not torch.allclose(o2.float().cpu(), e2.float(), atol=2e-2, rtol=2e-2):
+                errors.append(f"graph replay {rep}: out")
+        if _lib.device_error(clear=True) != 0:
+            errors.append("device error bits after the parity runs")
+        # bounded wait: rank 1 skips one call, rank 0's kernel must give up and report it
+        dist.barrier()
+        if rank == 0:
+            ar.partial_buffer(1, 8).zero_()
+            ar.reduce_norm(1, 8, None, dw, 1e-6)
+            torch.cuda.synchronize()
+            bits = _lib.device_error(clear=True)
+            if not bits & 16:
+                errors.append(f"expected the peer-timeout bit, got {bits}")
+        dist.barrier()
+        ar.close()
+    except Exception as e:  # report, never hang the other rank
+        errors.append(repr(e))
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    results[rank] = errors
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_fused_allreduce_two_gpus():
+    import torch.multiprocessing as mp
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _port()
+        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert dict(results) == {0: [], 1: []}, dict(results)

@@ -139,6 +139,24 @@ int kvb_paged_decode_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                           int batch, int num_q_heads, int num_kv_heads, int head_dim, float scale,
                           int num_splits, void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. The same decode attention for callers that
+ * cannot provide scratch memory: their interface passes only inputs and
+ * outputs (a plugin enqueue hook, a binding from a host language without a
+ * device allocator), or their device-memory budget is fixed at start-up. It
+ * allocates nothing: split-KV partials go to a built-in 8 MiB device array
+ * that every GPU loading the library keeps until the process exits. The first
+ * call on each device looks up that array's address (make that first call
+ * before any stream capture). Shapes whose partials would exceed 8 MiB
+ * (batch x num_q_heads x splits x 516 bytes) are rejected with kWorkspace (-3);
+ * num_splits = 1 needs no scratch. All calls on a device share the array, so
+ * calls whose kernels overlap on the GPU (unordered streams) race. */
+int kvb_paged_decode_attn_no_alloc(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache,
+                                   const void* v_cache, int64_t num_blocks, int64_t block_stride, int block_size,
+                                   const int32_t* block_tables, int64_t block_table_stride, int max_blocks_per_seq,
+                                   const int32_t* context_lens, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                                   int batch, int num_q_heads, int num_kv_heads, int head_dim, float scale,
+                                   int num_splits, void* stream);
+
 /* Causal varlen prefill attention (flash_attention_kvcache.py:73-79 =
  * flash_attn_varlen_func(..., causal=True, block_table)). Sequence b owns
  * queries [cu_seqlens_q[b], cu_seqlens_q[b+1]) and attends keys
@@ -207,8 +225,11 @@ int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void* residual_i
 /* ------------------------------------------------------------------ sampler */
 
 /* Sampler (sampler.py:7-66): token[b] = argmax_v(logits[b, v] / T[b] + g(b, v))
- * with Gumbel noise g from Philox4x32-10 keyed by *seed (device int32) and
- * counter b*vocab + v; T[b] == 0 is greedy argmax. Ties pick the lowest index.
+ * with Gumbel noise g = -log(-log(u)) from Philox4x32-10 keyed by *seed
+ * (device int32), counter (b*vocab + v)/4, u = (top 23 bits + 0.5) / 2^23;
+ * T[b] == 0 is greedy argmax. Ties pick the lowest index. Columns whose
+ * logit/T cannot reach the bound set by the largest logit skip the noise
+ * (exact: the noise is bounded by 24 ln 2).
  * logits bf16 [batch, vocab] with row stride; out int64 [batch]. The seed is
  * read, not advanced (the caller advances it, as sampler.py:59 does). */
 int kvb_sample(const void* logits, int64_t row_stride, const float* temperatures, const int32_t* seed,

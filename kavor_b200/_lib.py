@@ -33,6 +33,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_embedding": [P, P, P, I, I, L, L, L, P],
     "kvb_paged_decode_attn_workspace_size": [I, I, I, I, I, I, I, POINTER(c_size_t)],
     "kvb_paged_decode_attn": [P, L, L, P, P, L, L, I, P, L, I, P, P, L, L, I, I, I, I, F, I, P, c_size_t, P],
+    "kvb_paged_decode_attn_no_alloc": [P, L, L, P, P, L, L, I, P, L, I, P, P, L, L, I, I, I, I, F, I, P],
     "kvb_prefill_attn": [P, L, L, P, L, L, P, L, L, L, L, I, P, L, I, P, P, I, I, P, L, L, I, I, I, F, P],
     "kvb_sample": [P, L, P, P, P, I, I, P],
     "kvb_sample_partial": [P, L, P, P, P, P, I, I, L, L, P],

@@ -445,3 +445,125 @@ extern "C" int kvb_paged_decode_attn(const void* q, int64_t q_stride_t, int64_t 
   }
   return kOk;
 }
+
+// ---------------------------------------------------------------------------
+// Variant that allocates nothing and takes no scratch pointer.
+//
+// Some callers cannot hand the library a scratch buffer: their interface only
+// carries input and output pointers (a plugin "enqueue" hook, or a binding
+// from a host language that has no device allocator), or they run under a
+// fixed device-memory budget decided at start-up in which the library may not
+// request more memory. For them the split-KV partial results go to this
+// built-in area instead of a caller workspace. The area is a file-scope
+// device array of kStaticScratchBytes; every GPU that loads the library holds
+// it until the process exits. All calls on a device share it: two calls whose
+// kernels overlap on the GPU (different streams without ordering) race on it.
+// Nothing in it has to start at zero: every split writes all of its partials
+// before the merge reads them.
+static constexpr size_t kStaticScratchBytes = 8u << 20;  // 8 MiB
+static __device__ __align__(256) float g_decode_static_scratch[kStaticScratchBytes / sizeof(float)];
+
+namespace kvb {
+namespace {
+
+// Device address of the built-in area for the current device. The lookup runs
+// once per device, on the first call made while that device is current.
+int static_scratch_address(float** out) {
+  static float* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(kUnsupported, "kvb_paged_decode_attn_no_alloc: device index >= 64");
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc: cudaGetSymbolAddress");
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return kOk;
+}
+
+}  // namespace
+}  // namespace kvb
+
+extern "C" int kvb_paged_decode_attn_no_alloc(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                                              const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                              int64_t block_stride, int block_size, const int32_t* block_tables,
+                                              int64_t block_table_stride, int max_blocks_per_seq,
+                                              const int32_t* context_lens, void* out, int64_t out_stride_t,
+                                              int64_t out_stride_h, int batch, int num_q_heads, int num_kv_heads,
+                                              int head_dim, float scale, int num_splits, void* stream) {
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || num_blocks <= 0 ||
+      num_blocks >= INT32_MAX || block_size <= 0 || max_blocks_per_seq < 0 || num_splits < 0)
+    return set_error(kInvalid, "kvb_paged_decode_attn_no_alloc: bad sizes");
+  if (head_dim != kHD) return set_error(kUnsupported, "kvb_paged_decode_attn_no_alloc: head_dim must be 128");
+  if (block_size % kTile)
+    return set_error(kUnsupported, "kvb_paged_decode_attn_no_alloc: block_size must be a multiple of 64");
+  const int group = num_q_heads / num_kv_heads;
+  if (group > kMaxGroup)
+    return set_error(kUnsupported, "kvb_paged_decode_attn_no_alloc: more than 8 query heads per kv head");
+  if (batch == 0) return kOk;
+  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out)
+    return set_error(kInvalid, "kvb_paged_decode_attn_no_alloc: NULL pointer");
+  if (((uintptr_t)q & 3) || (q_stride_t & 1) || (q_stride_h & 1))
+    return set_error(kInvalid, "kvb_paged_decode_attn_no_alloc: q must be 4-byte aligned with even strides");
+  if (((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15) || block_stride % 8 ||
+      block_stride < (int64_t)block_size * num_kv_heads * kHD)
+    return set_error(kInvalid,
+                     "kvb_paged_decode_attn_no_alloc: cache must be 16-byte aligned with a full block stride");
+  const int max_tiles = (int)(((int64_t)max_blocks_per_seq * block_size + kTile - 1) / kTile);
+  const int splits = num_splits > 0 ? num_splits : choose_splits(batch, num_kv_heads, max_tiles, current_sms());
+  const size_t need = workspace_bytes(batch, num_q_heads, splits);
+  if (need > kStaticScratchBytes)
+    return set_error(kWorkspace,
+                     "kvb_paged_decode_attn_no_alloc: %d splits x %d sequences x %d heads need %zu bytes of scratch, "
+                     "the built-in area holds %zu; pass fewer splits (1 needs none) or use kvb_paged_decode_attn "
+                     "with a caller workspace",
+                     splits, batch, num_q_heads, need, kStaticScratchBytes);
+  float* ws = nullptr;
+  if (need > 0) {
+    int rc = static_scratch_address(&ws);
+    if (rc) return rc;
+  }
+
+  CUtensorMap kmap, vmap;
+  int rc = encode_kv_map(&kmap, k_cache, num_blocks, block_stride, block_size, num_kv_heads);
+  if (rc) return rc;
+  rc = encode_kv_map(&vmap, v_cache, num_blocks, block_stride, block_size, num_kv_heads);
+  if (rc) return rc;
+  rc = ensure_smem_attr();
+  if (rc) return rc;
+
+  DecodeArgs a;
+  a.q = (const bf16*)q;
+  a.q_st = q_stride_t;
+  a.q_sh = q_stride_h;
+  a.out = (bf16*)out;
+  a.o_st = out_stride_t;
+  a.o_sh = out_stride_h;
+  a.block_tables = block_tables;
+  a.bt_stride = block_table_stride;
+  a.max_blocks = max_blocks_per_seq;
+  a.context_lens = context_lens;
+  a.part_o = ws;
+  a.part_lse = ws ? ws + (size_t)batch * num_q_heads * splits * kHD : nullptr;
+  a.num_blocks = (int)num_blocks;
+  a.block_size = block_size;
+  a.hq = num_q_heads;
+  a.group = group;
+  a.num_splits = splits;
+  a.scale_log2 = scale * 1.4426950408889634f;
+
+  dim3 grid(splits, num_kv_heads, batch);
+  decode_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(kmap, vmap, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc launch");
+  if (splits > 1) {
+    decode_merge_kernel<<<dim3(num_q_heads, batch), kHD, 0, (cudaStream_t)stream>>>(
+        a.part_o, a.part_lse, (bf16*)out, out_stride_t, out_stride_h, num_q_heads, splits);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc merge launch");
+  }
+  return kOk;
+}

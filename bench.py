@@ -417,8 +417,9 @@ def run_ours(args) -> int:
             "gpu_launches": launches, "device_error_bits": dev_err,
         }
         print(json.dumps(line), flush=True)
-    runner.graphs.clear()
-    runner.graph_pool = None
+    # graphs hold NCCL work: every reference must be gone before the group is destroyed
+    del graph
+    runner.exit()
     torch.cuda.synchronize()
     barrier()
     dist.destroy_process_group()

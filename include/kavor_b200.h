@@ -174,20 +174,36 @@ int kvb_prefill_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h, cons
 
 /* --------------------------------------------------------------------- GEMM */
 
-/* Bytes of scratch kvb_gemm_bf16 needs for this shape (0 when it does not split
- * K). splits = 0 means the heuristic the call itself would pick. */
+/* Bytes of scratch kvb_gemm_bf16 needs for this shape: always 0 (a K split
+ * reduces through distributed shared memory); kept so callers can size and
+ * pass a workspace uniformly. */
 int kvb_gemm_workspace_size(int M, int N, int K, int splits, size_t* bytes);
 
 /* y[M, N] = x[M, K] * w[N, K]^T (F.linear of linear.py:50,73,157 and
  * embed_head.py:61) on tcgen05 tensor cores: bf16 operands, fp32 accumulation
  * in TMEM, bf16 result; rows of x, w, y with leading dimensions ldx, ldw, ldy
  * (elements; x and w rows 16-byte aligned). The weight is streamed once per
- * 256-token tile through TMA. When the heuristic splits K, fp32 partials go
- * through `workspace` (256-byte aligned, >= kvb_gemm_workspace_size bytes, its
- * first bytes are per-tile tickets that must be zero before the first call —
- * every call leaves them zero again); results are deterministic. */
+ * token tile (up to 256 tokens) through TMA. splits = 0 lets a cost model
+ * pick the token tile and the K split; splits in {1, 2, 4, 8, 16} forces the
+ * split (a thread-block cluster of that many CTAs whose fp32 parts are summed
+ * in a fixed order through distributed shared memory: deterministic).
+ * `workspace` is unused (may be NULL). */
 int kvb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
                   int splits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gate-up projection fused with SiluAndMul (linear.py:76-93 + activation.py:8-11):
+ * w is the [2 * inter, K] merged weight with rows [gate | up];
+ * y[M, inter] = bf16( silu(bf16(x w_gate^T)) * bf16(x w_up^T) ), fp32 inside —
+ * the reference's rounding points, without the [M, 2*inter] intermediate.
+ * Split and workspace rules as kvb_gemm_bf16. */
+int kvb_gemm_silu_workspace_size(int M, int inter, int K, int splits, size_t* bytes);
+int kvb_gemm_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int inter,
+                       int K, int splits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The tiling the GEMM picks for this shape on the current device (N = output
+ * width; gated = the fused SiLU form): plan[0] token tile, plan[1] K splits,
+ * plan[2] work units, plan[3] CTAs. */
+int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan);
 
 /* ---------------------------------------- tensor-parallel all-reduce (NVLink) */
 

@@ -280,6 +280,13 @@ def gemm_workspace_bytes(M: int, N: int, K: int, splits: int = 0) -> int:
     return int(n.value)
 
 
+def gemm_plan(M: int, N: int, K: int, splits: int = 0, gated: bool = False) -> dict:
+    """Tiling the GEMM picks for this shape (token tile, K splits, units, CTAs)."""
+    out = (ctypes.c_int * 4)()
+    _lib.call("kvb_gemm_plan", M, N, K, splits, int(gated), out)
+    return {"mt": out[0], "splits": out[1], "units": out[2], "grid": out[3]}
+
+
 def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
     """y = x @ weight^T on tcgen05 tensor cores (bf16 in/out, fp32 accumulate)."""
     _cuda(x, "x", _BF16)
@@ -294,6 +301,27 @@ def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
     ws = GEMM_WORKSPACE.reserve(need, x.device) if need else None
     _lib.call("kvb_gemm_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
               out.stride(0), M, N, K, splits, ws.data_ptr() if ws is not None else None,
+              ws.numel() if ws is not None else 0, _stream())
+    return out
+
+
+def gemm_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+              splits: int = 0) -> torch.Tensor:
+    """silu(x @ w_gate^T) * (x @ w_up^T) for the merged [gate | up] weight, one kernel."""
+    _cuda(x, "x", _BF16)
+    _cuda(weight, "weight", _BF16)
+    _req(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1] and weight.shape[0] % 2 == 0,
+         "gemm_silu: x [M, K], weight [2*I, K]")
+    _req(x.stride(1) == 1 and weight.stride(1) == 1, "gemm_silu: rows must be contiguous")
+    M, K = x.shape
+    inter = weight.shape[0] // 2
+    if out is None:
+        out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
+    n = ctypes.c_size_t(0)
+    _lib.call("kvb_gemm_silu_workspace_size", M, inter, K, splits, ctypes.byref(n))
+    ws = GEMM_WORKSPACE.reserve(int(n.value), x.device) if n.value else None
+    _lib.call("kvb_gemm_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
+              out.stride(0), M, inter, K, splits, ws.data_ptr() if ws is not None else None,
               ws.numel() if ws is not None else 0, _stream())
     return out
 

@@ -1,28 +1,37 @@
 // bf16 GEMM on the 5th-generation tensor cores: Y[M, N] = X[M, K] * W[N, K]^T
 // (F.linear of linear.py:50,73,157 and embed_head.py:61), fp32 accumulation in
-// TMEM, bf16 output.
+// TMEM, bf16 output; and the gate-up projection fused with SiluAndMul.
 //
 // Orientation ("swap AB"): the UMMA A operand is a 128-row slab of the weight
 // W (128 output features), the B operand is a tile of MT token rows of X, so
 // the accumulator D[feature, token] lives in 128 TMEM lanes x MT columns. At
-// decode batch sizes (M <= 256 tokens) one tile covers every token and the
-// kernel streams each weight byte exactly once — the GEMM is HBM-bound and its
-// roofline is weight bytes / HBM bandwidth. Larger M is tiled in MT = 256
-// token chunks.
+// decode batch sizes (M <= 256) the whole batch is one token tile and every
+// weight byte is read from HBM exactly once.
 //
-//   warp 0      TMA producer: W box {64 K, 128 rows} + X box {64 K, MT rows},
-//               128-byte swizzle, into a `stages`-deep mbarrier ring;
-//   warp 1      allocates TMEM, one elected thread issues
+// A CTA is warp-specialised:
+//   warp 0      TMA producer: W box {64 K, 128 rows} (+ the up-half box when
+//               gated) + X box {64 K, MT rows}, 128-byte swizzle, into a
+//               `stages`-deep mbarrier ring;
+//   warp 1      allocates TMEM; one thread issues
 //               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=MT, K=16) x4 per
-//               stage and tcgen05.commit's the stage back to the producer;
-//   warps 2..5  epilogue: tcgen05.ld 32x32b of their TMEM lane quarter,
-//               thread = output feature, columns = tokens; coalesced bf16
-//               stores (or fp32 split-K partials).
-// Split-K: the K range of a weight slab is cut into `splits` parts so that
-// (slabs x splits) fills the 148 SMs in whole waves; every part stores fp32
-// partials to the workspace and the last CTA to finish a slab (atomic ticket)
-// sums the parts in split order (deterministic) and writes bf16, then resets
-// its ticket to zero for the next call.
+//               stage (x8 gated), tcgen05.commit's each stage back to the
+//               producer and each finished accumulator to the epilogue;
+//   warps 2..5  epilogue, one TMEM lane quarter each (tcgen05.ld 32x32b).
+//
+// Two schedules, chosen with the tile MT by a cost model:
+//   persistent  (no K split): CTAs walk a static list of (weight slab, token
+//               tile) units; two TMEM accumulators, so the MMAs of the next
+//               unit overlap this unit's epilogue, which goes through a
+//               per-warp shared-memory transpose and leaves as 64-byte token
+//               rows;
+//   cluster     (K split over C = 2..16 CTAs of one thread-block cluster, one
+//               unit per CTA): when its MMAs are done every CTA pushes its fp32
+//               accumulator through distributed shared memory into the CTAs
+//               that own each 128/C-feature slice (the stage ring, idle by
+//               then, is the landing buffer), and each owner sums the C parts
+//               in cluster-rank order — deterministic — and writes bf16. No
+//               global scratch memory and no atomics.
+// No cluster multicast is used anywhere (multi-GPU safe).
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -38,16 +47,17 @@ constexpr int kBN = 128;         // weight rows per slab = UMMA M
 constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiWarp0 = 2;
 constexpr int kABytes = kBN * kBK * 2;  // 16 KB
+constexpr int kMaxCluster = 16;
 
 struct GemmArgs {
   bf16* y;
   int64_t ldy;
-  float* partial;   // [splits][m_pad][n_pad] fp32 when splits > 1
-  int* tickets;     // [n_tiles * m_tiles]
   int M, N;
   int n_tiles, m_tiles, splits, kb_total, kb_per_split;
-  int n_pad, m_pad;
+  int units;
+  int up_row0;      // gated: first weight row of the up half (= output width)
   uint32_t idesc;
+  int vec_out;      // y rows are 16-byte aligned
 };
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
@@ -79,7 +89,28 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 consecutive TMEM columns of this warp's 32 lanes -> 32 registers per thread.
+// ------------------------------------------------------------ cluster helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster; release/acquire orders the
+// distributed-shared-memory stores around it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// 32 (or 16) consecutive TMEM columns of this warp's 32 lanes -> registers.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
@@ -108,47 +139,77 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int MT>
+constexpr int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// G (gated): every unit multiplies the token tile with TWO weight slabs — the
+// gate rows [n0, n0+128) and the up rows [I + n0, I + n0 + 128) of the
+// [gate | up] weight (linear.py:76-93 layout) — into two accumulators, and the
+// epilogue writes bf16(silu(gate) * up) (activation.py:8-11).
+// CL (cluster split-K): one unit per CTA, one accumulator.
+template <int MT, bool G, bool CL>
 struct Cfg {
+  static constexpr int kA = G ? 2 : 1;                      // weight slabs per unit
   static constexpr int kBBytes = MT * kBK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBudget = MT <= 64 ? 110 * 1024 : 200 * 1024;  // two CTAs per SM when MT <= 64
+  static constexpr int kStageBytes = kA * kABytes + kBBytes;
+  static constexpr int kPerSm = (!G && MT <= 64) ? 2 : 1;   // CTAs resident per SM
+  static constexpr int kBudget = kPerSm == 2 ? 96 * 1024 : 192 * 1024;
   static constexpr int kStagesRaw = kBudget / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
-  static constexpr int kTmemCols = MT < 32 ? 32 : MT;
-  static constexpr int kSmem = kStages * kStageBytes + 1024;
+  static constexpr int kChunk = MT < 32 ? 16 : 32;          // tokens per TMEM load
+  static constexpr int kOutBytes = CL ? 0 : 4 * 32 * kChunk * 2;  // per-warp transpose tiles
+  static constexpr int kAccCols = kA * MT;                  // one accumulator (gate [+ up])
+  static constexpr int kTmemCols = pow2_at_least(CL ? kAccCols : 2 * kAccCols);
+  static constexpr int kPitch = MT + 4;                     // fp32 row pitch of the cluster landing buffer
+  static constexpr int kRedBytes = kA * kBN * kPitch * 4;   // [slab][rank][feature/C][kPitch], any C
+  static constexpr int kSmem = kStages * kStageBytes + kOutBytes + 1024;
+  static_assert(!CL || kRedBytes <= kStages * kStageBytes, "landing buffer must fit the stage ring");
 };
 
-template <int MT>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ float silu_mul_rounded(float g, float u) {
+  // the reference rounds the projection to bf16 before SiluAndMul
+  g = bf16_round(g);
+  u = bf16_round(u);
+  return g / (1.f + __expf(-g)) * u;
+}
+
+__device__ __forceinline__ void unit_coords(const GemmArgs& a, int u, int& n_tile, int& m_tile, int& split, int& kb0,
+                                            int& nkb) {
+  split = u % a.splits;  // = %cluster_ctarank in the cluster schedule (cluster dims {splits, 1, 1})
+  const int t = u / a.splits;
+  m_tile = t % a.m_tiles;
+  n_tile = t / a.m_tiles;
+  kb0 = split * a.kb_per_split;
+  nkb = max(0, min(kb0 + a.kb_per_split, a.kb_total) - kb0);
+}
+
+template <int MT, bool G, bool CL>
+__global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ GemmArgs a) {
-  using C = Cfg<MT>;
+  using C = Cfg<MT, G, CL>;
+  constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[C::kStages];
-  __shared__ __align__(8) uint64_t empty_bar[C::kStages];
-  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_s;
-  __shared__ int last_s;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int bid = blockIdx.x;
-  const int split = bid % a.splits;
-  bid /= a.splits;
-  const int m_tile = bid % a.m_tiles;
-  const int n_tile = bid / a.m_tiles;
-  const int kb0 = split * a.kb_per_split;
-  const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
-  const int nkb = kb1 - kb0;
-  const int n0 = n_tile * kBN, m0 = m_tile * MT;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
-    mbar_init(smem_u32(&accum_bar), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -160,107 +221,212 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_d = tmem_base_s;
+  const uint32_t tmem = tmem_base_s;
+  bool dead = false;  // a bounded wait gave up: skip the work, keep every barrier balanced
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    if (lane == 0 && nkb > 0) {
+    if (lane == 0) {
       prefetch_tensormap(&wmap);
       prefetch_tensormap(&xmap);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::kStages;
-        if (i >= C::kStages && !mbar_wait(smem_u32(&empty_bar[s]), ((i / C::kStages) - 1) & 1, &g_err_gemm)) break;
-        const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
-        const uint32_t fb = smem_u32(&full_bar[s]);
-        mbar_arrive_expect_tx(fb, C::kStageBytes);
-        tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n0, fb);
-        tma_load_2d(sa + kABytes, &xmap, (kb0 + i) * kBK, m0, fb);
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        int n_tile, m_tile, split, kb0, nkb;
+        unit_coords(a, u, n_tile, m_tile, split, kb0, nkb);
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(smem_u32(&empty_bar[s]), ((it / S) - 1) & 1, &g_err_gemm)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t fb = smem_u32(&full_bar[s]);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n_tile * kBN, fb);
+          if constexpr (G) tma_load_2d(sa + kABytes, &wmap, (kb0 + i) * kBK, a.up_row0 + n_tile * kBN, fb);
+          tma_load_2d(sa + C::kA * kABytes, &xmap, (kb0 + i) * kBK, m_tile * MT, fb);
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && nkb > 0) {
+    if (lane == 0) {
+      int it = 0, local = 0;
       bool ok = true;
-      for (int i = 0; i < nkb && ok; ++i) {
-        const int s = i % C::kStages;
-        if (!mbar_wait(smem_u32(&full_bar[s]), (i / C::kStages) & 1, &g_err_gemm)) {
-          ok = false;
-          break;
-        }
+      for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x, ++local) {
+        int n_tile, m_tile, split, kb0, nkb;
+        unit_coords(a, u, n_tile, m_tile, split, kb0, nkb);
+        const int buf = local & 1;
+        if (local >= 2 && !mbar_wait(smem_u32(&acc_empty[buf]), ((local >> 1) - 1) & 1, &g_err_gemm)) break;
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
-        const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sa + kABytes);
+        const uint32_t d = tmem + buf * C::kAccCols;
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&full_bar[s]), (it / S) & 1, &g_err_gemm)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
+          const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sa + C::kA * kABytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // +32 bytes along K inside the swizzle atom = +2 in the address field
-          umma_bf16(tmem_d, da + 2 * k, db + 2 * k, a.idesc, (i > 0 || k > 0) ? 1u : 0u);
-        umma_commit(smem_u32(&empty_bar[s]));
+          for (int k = 0; k < kBK / 16; ++k)  // +32 bytes along K inside the swizzle atom = +2 in the address field
+            umma_bf16(d, da + 2 * k, db + 2 * k, a.idesc, (i > 0 || k > 0) ? 1u : 0u);
+          if constexpr (G) {
+            const uint64_t du = smem_desc_sw128(sa + kABytes);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              umma_bf16(d + MT, du + 2 * k, db + 2 * k, a.idesc, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty_bar[s]));
+        }
+        umma_commit(smem_u32(&acc_full[buf]));
       }
-      umma_commit(smem_u32(&accum_bar));
-      // do not leave the CTA (and free TMEM) with MMAs in flight
-      mbar_wait(smem_u32(&accum_bar), 0, &g_err_gemm);
+      // no MMA may still run when TMEM is freed (or, clustered, when the ring
+      // becomes a landing buffer): wait for the last accumulator
+      if (local > 0) mbar_wait(smem_u32(&acc_full[(local - 1) & 1]), ((local - 1) >> 1) & 1, &g_err_gemm);
     }
-  } else {
-    // ---------------------------------------------------------------- epilogue
+  } else if constexpr (!CL) {
+    // ---------------------------------------------------------------- epilogue (persistent)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int n = n0 + q * 32 + lane;
-    const bool ok = nkb > 0 && mbar_wait(smem_u32(&accum_bar), 0, &g_err_gemm);
-    tc_fence_after();
-    const uint32_t trow = tmem_d + ((uint32_t)(q * 32) << 16);
-    if (a.splits == 1) {
-      if (ok) {
+    constexpr int CH = C::kChunk;
+    bf16* tile_out = reinterpret_cast<bf16*>(smem + S * C::kStageBytes) + (warp - kEpiWarp0) * 32 * CH;
+    int local = 0;
+    for (int u = blockIdx.x; u < a.units; u += gridDim.x, ++local) {
+      int n_tile, m_tile, split, kb0, nkb;
+      unit_coords(a, u, n_tile, m_tile, split, kb0, nkb);
+      const int buf = local & 1;
+      const int n0 = n_tile * kBN, m0 = m_tile * MT;
+      if (!dead && !mbar_wait(smem_u32(&acc_full[buf]), (local >> 1) & 1, &g_err_gemm)) dead = true;
+      if (dead) continue;
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + buf * C::kAccCols;
 #pragma unroll 1
-        for (int c = 0; c < MT; c += (MT < 32 ? 16 : 32)) {
-          float v[32];
-          if constexpr (MT < 32) tmem_ld16(trow + c, v); else tmem_ld32(trow + c, v);
-          if (n < a.N) {
+      for (int c = 0; c < MT; c += CH) {
+        float v[32];
+        if constexpr (CH == 16) tmem_ld16(trow + c, v); else tmem_ld32(trow + c, v);
+        if constexpr (G) {
+          float w[32];
+          if constexpr (CH == 16) tmem_ld16(trow + MT + c, w); else tmem_ld32(trow + MT + c, w);
 #pragma unroll
-            for (int j = 0; j < (MT < 32 ? 16 : 32); ++j) {
-              const int m = m0 + c + j;
-              if (m < a.M) a.y[(int64_t)m * a.ldy + n] = __float2bfloat16_rn(v[j]);
-            }
+          for (int j = 0; j < CH; ++j) v[j] = silu_mul_rounded(v[j], w[j]);
+        }
+        // transpose through shared memory: tile_out[token][feature], 64-byte rows
+#pragma unroll
+        for (int j = 0; j < CH; ++j) tile_out[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+        __syncwarp();
+        const int m = m0 + c + lane;
+        const int nb = n0 + q * 32;
+        if (lane < CH && m < a.M) {
+          bf16* yr = a.y + (int64_t)m * a.ldy + nb;
+          const bf16* src = tile_out + lane * 32;
+          if (a.vec_out && nb + 32 <= a.N) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(yr)[e] = reinterpret_cast<const uint4*>(src)[e];
+          } else {
+            for (int e = 0; e < 32 && nb + e < a.N; ++e) yr[e] = src[e];
           }
         }
+        __syncwarp();
       }
-    } else {
-      // fp32 partial of this split, then the last split of the slab reduces
-      float* part = a.partial + ((int64_t)split * a.m_pad + m0) * a.n_pad + n;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (cluster), part 1
+    if (!mbar_wait(smem_u32(&acc_full[0]), 0, &g_err_gemm)) dead = true;
+    tc_fence_after();
+  }
+
+  if constexpr (CL) {
+    // part 2: every CTA's MMAs are complete after this barrier, so every stage
+    // ring is free; push the fp32 accumulator slices to their owners
+    __syncwarp();
+    cluster_sync_all();
+    const int Cn = a.splits;
+    const int fpc = kBN / Cn;  // features owned by each cluster rank
+    const uint32_t rank = cluster_rank();
+    int n_tile, m_tile, split, kb0, nkb;
+    unit_coords(a, blockIdx.x, n_tile, m_tile, split, kb0, nkb);
+    const uint32_t red = smem_u32(smem);
+    if (warp >= kEpiWarp0 && !dead) {
+      constexpr int CH = C::kChunk;
+      const int q = warp & 3;
+      const int f = q * 32 + lane;
+      const uint32_t owner = (uint32_t)(f / fpc);
+      const int fl = f % fpc;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < MT; c += (MT < 32 ? 16 : 32)) {
-        float v[32];
-        if (ok) {
-          if constexpr (MT < 32) tmem_ld16(trow + c, v); else tmem_ld32(trow + c, v);
+      for (int h = 0; h < C::kA; ++h) {
+        const uint32_t dst = map_to_rank(red + (uint32_t)((((h * Cn + (int)rank) * fpc + fl) * C::kPitch) * 4), owner);
+#pragma unroll 1
+        for (int c = 0; c < MT; c += CH) {
+          float v[32];
+          if (nkb > 0) {
+            if constexpr (CH == 16) tmem_ld16(trow + h * MT + c, v); else tmem_ld32(trow + h * MT + c, v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) v[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < CH; j += 4) st_cluster_v4(dst + (uint32_t)(c + j) * 4, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync_all();
+    // part 3: this CTA owns features [rank * fpc, (rank + 1) * fpc) of the tile
+    if (warp >= kEpiWarp0 && !dead) {
+      const float* rf = reinterpret_cast<const float*>(smem);
+      const int e = threadIdx.x - kEpiWarp0 * 32;
+      const int groups = (fpc / 8) * MT;
+      const int n0 = n_tile * kBN + (int)rank * fpc, m0 = m_tile * MT;
+#pragma unroll 1
+      for (int g = e; g < groups; g += 128) {
+        const int ml = g % MT, fg = g / MT;
+        const int m = m0 + ml;
+        if (m >= a.M) continue;
+        float acc[8], acu[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = acu[j] = 0.f;
+#pragma unroll 1
+        for (int s = 0; s < Cn; ++s) {
+          const float* p = rf + ((s * fpc + fg * 8) * C::kPitch + ml);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += p[j * C::kPitch];
+          if constexpr (G) {
+            const float* pu = p + Cn * fpc * C::kPitch;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acu[j] += pu[j * C::kPitch];
+          }
+        }
+        if constexpr (G) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = silu_mul_rounded(acc[j], acu[j]);
+        }
+        const int n = n0 + fg * 8;
+        bf16* yr = a.y + (int64_t)m * a.ldy + n;
+        if (a.vec_out && n + 8 <= a.N) {
+          uint4 pk;
+          __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h2[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+          *reinterpret_cast<uint4*>(yr) = pk;
         } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          for (int j = 0; j < 8 && n + j < a.N; ++j) yr[j] = __float2bfloat16_rn(acc[j]);
         }
-#pragma unroll
-        for (int j = 0; j < (MT < 32 ? 16 : 32); ++j) part[(int64_t)(c + j) * a.n_pad] = v[j];
-      }
-      __threadfence();
-      named_bar_sync(1, 128);
-      int* ticket = a.tickets + n_tile * a.m_tiles + m_tile;
-      if (threadIdx.x == kEpiWarp0 * 32) last_s = atomicAdd(ticket, 1) == a.splits - 1;
-      named_bar_sync(1, 128);
-      if (last_s) {
-        __threadfence();
-        const float* base = a.partial + (int64_t)m0 * a.n_pad + n;
-        const int64_t sstride = (int64_t)a.m_pad * a.n_pad;
-#pragma unroll 1
-        for (int j = 0; j < MT; ++j) {
-          const int m = m0 + j;
-          float acc = 0.f;
-          for (int s = 0; s < a.splits; ++s) acc += __ldcg(base + s * sstride + (int64_t)j * a.n_pad);
-          if (n < a.N && m < a.M) a.y[(int64_t)m * a.ldy + n] = __float2bfloat16_rn(acc);
-        }
-        if (threadIdx.x == kEpiWarp0 * 32) *ticket = 0;
       }
     }
   }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(C::kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
   }
 }
 
@@ -290,95 +456,197 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
   return kOk;
 }
 
-int pick_mt(int M) {
-  if (M <= 16) return 16;
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
-}
-
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
   if (!cached[dev]) {
     int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) cudaGetLastError();
     cached[dev] = n > 0 ? n : 148;
   }
   return cached[dev];
 }
 
 struct Plan {
-  int mt, n_tiles, m_tiles, splits, kb_total, kb_per_split, n_pad, m_pad;
-  size_t ws_bytes;
+  int mt, n_tiles, m_tiles, splits, kb_total, kb_per_split, units, grid;
 };
 
-// Split count from a two-term cost model: a split-K plan with s parts runs
-// tiles*s CTAs in ceil(tiles*s / slots) waves; its time is the larger of
-// (all bytes it moves) / HBM bandwidth and (waves x bytes one CTA streams) /
-// per-SM streaming bandwidth. fp32 partials (s > 1) count at L2 bandwidth.
-Plan make_plan(int M, int N, int K, int splits_req) {
+struct TileShape {
+  int mt, stages, per_sm;
+};
+
+constexpr TileShape kShapes[] = {{16, Cfg<16, false, false>::kStages, Cfg<16, false, false>::kPerSm},
+                                 {32, Cfg<32, false, false>::kStages, Cfg<32, false, false>::kPerSm},
+                                 {64, Cfg<64, false, false>::kStages, Cfg<64, false, false>::kPerSm},
+                                 {128, Cfg<128, false, false>::kStages, Cfg<128, false, false>::kPerSm},
+                                 {256, Cfg<256, false, false>::kStages, Cfg<256, false, false>::kPerSm}};
+constexpr TileShape kGatedShapes[] = {{16, Cfg<16, true, false>::kStages, Cfg<16, true, false>::kPerSm},
+                                      {32, Cfg<32, true, false>::kStages, Cfg<32, true, false>::kPerSm},
+                                      {64, Cfg<64, true, false>::kStages, Cfg<64, true, false>::kPerSm},
+                                      {128, Cfg<128, true, false>::kStages, Cfg<128, true, false>::kPerSm}};
+
+Plan finish_plan(int M, int N, int K, int mt, int per_sm, int splits) {
   Plan p;
-  p.mt = pick_mt(M);
+  p.mt = mt;
   p.n_tiles = (N + kBN - 1) / kBN;
-  p.m_tiles = (M + p.mt - 1) / p.mt;
+  p.m_tiles = (M + mt - 1) / mt;
   p.kb_total = (K + kBK - 1) / kBK;
-  const int per_sm = p.mt <= 64 ? 2 : 1;
+  if (splits > p.kb_total) splits = p.kb_total;
+  if (splits > kMaxCluster) splits = kMaxCluster;
+  if (splits < 1) splits = 1;
+  p.splits = splits;
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.units = p.n_tiles * p.m_tiles * p.splits;
   const int slots = sm_count() * per_sm;
-  const int tiles = p.n_tiles * p.m_tiles;
-  int best = 1;
-  if (splits_req > 0) {
-    best = splits_req;
-  } else {
-    const double hbm = 6.5e12, l2 = 20e12, per_sm_bw = 60e9;
-    double best_t = 1e30;
-    const int max_s = p.kb_total / 4 > 1 ? p.kb_total / 4 : 1;
-    for (int s = 1; s <= 32 && s <= max_s; ++s) {
-      const int kb = (p.kb_total + s - 1) / s;
-      const int se = (p.kb_total + kb - 1) / kb;
-      const double unit = (double)(kBN + p.mt) * kb * kBK * 2;
-      const double part = se > 1 ? 2.0 * p.mt * kBN * 4 : 0.0;
-      const int units = tiles * se;
-      const int waves = (units + slots - 1) / slots;
-      const double t_mem = (double)units * unit / hbm + (double)units * part / l2;
-      const double t_sm = (double)waves * (unit + part) / per_sm_bw;
-      const double t = t_mem > t_sm ? t_mem : t_sm;
-      if (t < best_t * 0.97) {
-        best_t = t;
-        best = se;
-      }
-    }
-  }
-  if (best > p.kb_total) best = p.kb_total;
-  p.kb_per_split = (p.kb_total + best - 1) / best;
-  p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
-  p.n_pad = p.n_tiles * kBN;
-  p.m_pad = p.m_tiles * p.mt;
-  p.ws_bytes = 0;
-  if (p.splits > 1) {
-    const size_t tick = ((size_t)tiles * sizeof(int) + 255) & ~size_t(255);
-    p.ws_bytes = tick + (size_t)p.splits * p.m_pad * p.n_pad * sizeof(float);
-  }
+  p.grid = (p.splits > 1 || p.units < slots) ? p.units : slots;
   return p;
 }
 
-template <int MT>
-int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, GemmArgs& a, cudaStream_t stream) {
-  using C = Cfg<MT>;
+// Cost model (microseconds). Per K-block a CTA is bound by the tensor pipe
+// (4 MMAs of 128 x MT x 16 per weight slab, 128 cycles each at MT = 256) or by
+// what it can pull through TMA (~200 GB/s per SM); a CTA also pays a pipeline
+// fill. Persistent: ceil(units / grid) units back to back, epilogues hidden
+// except the last. Cluster: waves of clusters, each paying the DSMEM exchange
+// (~60 GB/s per SM) and the reduction. The whole GEMM is also bound by HBM:
+// the weight once per token tile (no reuse across tiles is assumed), the
+// tokens and the output.
+double plan_cost(const Plan& p, int M, int N, int K, int per_sm, int slabs) {
+  const double clk = 1.9e3;  // cycles per us
+  const int nsm = sm_count();
+  const double t_mma = 4.0 * slabs * 128.0 * (p.mt < 32 ? 32 : p.mt) / 256.0 / clk;
+  const double kb_bytes = slabs * (double)kABytes + (double)p.mt * kBK * 2;
+  const double t_tma = kb_bytes / (per_sm == 2 ? 120e3 : 200e3);
+  const double t_kb = t_mma > t_tma ? t_mma : t_tma;
+  const double fill = 1.2;
+  double t_cta;
+  if (p.splits == 1) {
+    const int upc = (p.units + p.grid - 1) / p.grid;
+    t_cta = fill + upc * p.kb_per_split * t_kb + p.mt * kBN * 2.0 / 150e3;
+  } else {
+    const int per_wave = (nsm * per_sm / p.splits) * p.splits;
+    const int waves = (p.units + per_wave - 1) / per_wave;
+    const double xchg = slabs * 128.0 * p.mt * 4.0 * (p.splits - 1) / p.splits / 60e3 + 0.5;
+    t_cta = waves * (fill + p.kb_per_split * t_kb + xchg);
+  }
+  const double hbm = ((double)slabs * N * K * p.m_tiles + (double)M * K + (double)M * N) * 2.0 / 6.5e6;
+  return t_cta > hbm ? t_cta : hbm;
+}
+
+// N is the OUTPUT width (for the gated form: the intermediate size I).
+// splits_req > 0 forces the K split (cluster size, at most 16).
+Plan make_plan(int M, int N, int K, int splits_req, bool gated = false) {
+  Plan best{};
+  double best_t = 1e30;
+  const int slabs = gated ? 2 : 1;
+  const TileShape* shapes = gated ? kGatedShapes : kShapes;
+  const int nshapes = gated ? 4 : 5;
+  static const int kSplits[] = {1, 2, 4, 8, 16};
+  for (int si = 0; si < nshapes; ++si) {
+    const TileShape& sh = shapes[si];
+    if (sh.mt > 16 && sh.mt >= 2 * M) continue;  // a token tile far above the batch wastes tensor work
+    for (int s : kSplits) {
+      if (splits_req > 0 && s != splits_req) continue;
+      Plan p = finish_plan(M, N, K, sh.mt, sh.per_sm, s);
+      if (p.splits != s) continue;
+      if (p.splits > 1 && (int64_t)(p.splits - 1) * p.kb_per_split >= p.kb_total) continue;  // an empty part
+      const double t = plan_cost(p, M, N, K, sh.per_sm, slabs);
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best = p;
+      }
+    }
+  }
+  if (best.mt == 0) {  // a forced split that no tile accepts: fall back to the heuristic
+    return make_plan(M, N, K, 0, gated);
+  }
+  return best;
+}
+
+template <int MT, bool G, bool CL>
+int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, GemmArgs& a, int grid, cudaStream_t stream) {
+  using C = Cfg<MT, G, CL>;
   static unsigned long long done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !((done >> dev) & 1ull)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (e != cudaSuccess) return cuda_status(e, "gemm smem attribute");
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<MT, G, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e == cudaSuccess && CL)
+      e = cudaFuncSetAttribute(gemm_kernel<MT, G, CL>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_status(e, "gemm kernel attributes");
     if (dev < 64) done |= 1ull << dev;
   }
   a.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MT >> 3) << 17) | ((uint32_t)(kBN >> 4) << 24);
-  const unsigned grid = (unsigned)(a.n_tiles * a.m_tiles * a.splits);
-  gemm_kernel<MT><<<grid, kThreads, C::kSmem, stream>>>(wmap, xmap, a);
-  return cuda_status(cudaGetLastError(), "kvb_gemm_bf16 launch");
+  if constexpr (!CL) {
+    gemm_kernel<MT, G, CL><<<grid, kThreads, C::kSmem, stream>>>(wmap, xmap, a);
+    return cuda_status(cudaGetLastError(), "kvb_gemm launch");
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, gemm_kernel<MT, G, CL>, wmap, xmap, a), "kvb_gemm cluster launch");
+  }
+}
+
+template <int MT, bool G>
+int launch_mt(const CUtensorMap& wmap, const CUtensorMap& xmap, GemmArgs& a, int grid, cudaStream_t stream) {
+  return a.splits > 1 ? launch<MT, G, true>(wmap, xmap, a, grid, stream) : launch<MT, G, false>(wmap, xmap, a, grid, stream);
+}
+
+// y[M, n_out] = x w^T (gated: bf16(silu(x w_gate^T) * (x w_up^T)), w = [gate | up]
+// with n_out rows each).
+int run_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int n_out, int K,
+             int splits, void* stream, bool gated, const char* name) {
+  if (M < 0 || n_out <= 0 || K <= 0 || splits < 0 || ldx < K || ldw < K || ldy < n_out)
+    return set_error(kInvalid, "%s: bad sizes or leading dimensions", name);
+  if (M == 0) return kOk;
+  if (!x || !w || !y) return set_error(kInvalid, "%s: NULL pointer", name);
+  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ldx % 8 || ldw % 8 || K % 8)
+    return set_error(kInvalid, "%s: x/w rows must be 16-byte aligned (K, ldx, ldw multiples of 8)", name);
+  Plan p = make_plan(M, n_out, K, splits, gated);
+  CUtensorMap wmap, xmap;
+  int rc = encode_2d(&wmap, w, (int64_t)n_out * (gated ? 2 : 1), K, ldw, kBN);
+  if (rc) return rc;
+  rc = encode_2d(&xmap, x, M, K, ldx, p.mt);
+  if (rc) return rc;
+  GemmArgs a;
+  a.y = (bf16*)y;
+  a.ldy = ldy;
+  a.M = M;
+  a.N = n_out;
+  a.n_tiles = p.n_tiles;
+  a.m_tiles = p.m_tiles;
+  a.splits = p.splits;
+  a.kb_total = p.kb_total;
+  a.kb_per_split = p.kb_per_split;
+  a.units = p.units;
+  a.up_row0 = n_out;
+  a.vec_out = ((uintptr_t)y & 15) == 0 && ldy % 8 == 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (gated) {
+    switch (p.mt) {
+      case 16: return launch_mt<16, true>(wmap, xmap, a, p.grid, st);
+      case 32: return launch_mt<32, true>(wmap, xmap, a, p.grid, st);
+      case 64: return launch_mt<64, true>(wmap, xmap, a, p.grid, st);
+      default: return launch_mt<128, true>(wmap, xmap, a, p.grid, st);
+    }
+  }
+  switch (p.mt) {
+    case 16: return launch_mt<16, false>(wmap, xmap, a, p.grid, st);
+    case 32: return launch_mt<32, false>(wmap, xmap, a, p.grid, st);
+    case 64: return launch_mt<64, false>(wmap, xmap, a, p.grid, st);
+    case 128: return launch_mt<128, false>(wmap, xmap, a, p.grid, st);
+    default: return launch_mt<256, false>(wmap, xmap, a, p.grid, st);
+  }
 }
 
 }  // namespace
@@ -388,48 +656,37 @@ using namespace kvb;
 
 extern "C" int kvb_gemm_workspace_size(int M, int N, int K, int splits, size_t* bytes) {
   if (!bytes || M < 0 || N <= 0 || K <= 0 || splits < 0) return set_error(kInvalid, "kvb_gemm_workspace_size: bad sizes");
-  *bytes = M == 0 ? 0 : make_plan(M, N, K, splits).ws_bytes;
+  *bytes = 0;  // the K split reduces through distributed shared memory
   return kOk;
 }
 
 extern "C" int kvb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
                              int N, int K, int splits, void* workspace, size_t workspace_bytes, void* stream) {
-  if (M < 0 || N <= 0 || K <= 0 || splits < 0 || ldx < K || ldw < K || ldy < N)
-    return set_error(kInvalid, "kvb_gemm_bf16: bad sizes or leading dimensions");
-  if (M == 0) return kOk;
-  if (!x || !w || !y) return set_error(kInvalid, "kvb_gemm_bf16: NULL pointer");
-  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ldx % 8 || ldw % 8 || K % 8)
-    return set_error(kInvalid, "kvb_gemm_bf16: x/w rows must be 16-byte aligned (K, ldx, ldw multiples of 8)");
-  Plan p = make_plan(M, N, K, splits);
-  if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes || ((uintptr_t)workspace & 255)))
-    return set_error(kWorkspace, "kvb_gemm_bf16: workspace of %zu bytes (256-byte aligned, tickets zeroed) needed, %zu given",
-                     p.ws_bytes, workspace_bytes);
-  CUtensorMap wmap, xmap;
-  int rc = encode_2d(&wmap, w, N, K, ldw, kBN);
-  if (rc) return rc;
-  rc = encode_2d(&xmap, x, M, K, ldx, p.mt);
-  if (rc) return rc;
-  GemmArgs a;
-  a.y = (bf16*)y;
-  a.ldy = ldy;
-  a.M = M;
-  a.N = N;
-  a.n_tiles = p.n_tiles;
-  a.m_tiles = p.m_tiles;
-  a.splits = p.splits;
-  a.kb_total = p.kb_total;
-  a.kb_per_split = p.kb_per_split;
-  a.n_pad = p.n_pad;
-  a.m_pad = p.m_pad;
-  const size_t tick = ((size_t)p.n_tiles * p.m_tiles * sizeof(int) + 255) & ~size_t(255);
-  a.tickets = p.splits > 1 ? (int*)workspace : nullptr;
-  a.partial = p.splits > 1 ? (float*)((uint8_t*)workspace + tick) : nullptr;
-  cudaStream_t st = (cudaStream_t)stream;
-  switch (p.mt) {
-    case 16: return launch<16>(wmap, xmap, a, st);
-    case 32: return launch<32>(wmap, xmap, a, st);
-    case 64: return launch<64>(wmap, xmap, a, st);
-    case 128: return launch<128>(wmap, xmap, a, st);
-    default: return launch<256>(wmap, xmap, a, st);
-  }
+  (void)workspace;
+  (void)workspace_bytes;
+  return run_gemm(x, ldx, w, ldw, y, ldy, M, N, K, splits, stream, false, "kvb_gemm_bf16");
+}
+
+extern "C" int kvb_gemm_silu_workspace_size(int M, int inter, int K, int splits, size_t* bytes) {
+  if (!bytes || M < 0 || inter <= 0 || K <= 0 || splits < 0)
+    return set_error(kInvalid, "kvb_gemm_silu_workspace_size: bad sizes");
+  *bytes = 0;
+  return kOk;
+}
+
+extern "C" int kvb_gemm_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
+                                  int inter, int K, int splits, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  return run_gemm(x, ldx, w, ldw, y, ldy, M, inter, K, splits, stream, true, "kvb_gemm_silu_bf16");
+}
+
+extern "C" int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan) {
+  if (!plan || M <= 0 || N <= 0 || K <= 0 || splits < 0) return set_error(kInvalid, "kvb_gemm_plan: bad sizes");
+  const Plan p = make_plan(M, N, K, splits, gated != 0);
+  plan[0] = p.mt;
+  plan[1] = p.splits;
+  plan[2] = p.units;
+  plan[3] = p.grid;
+  return kOk;
 }

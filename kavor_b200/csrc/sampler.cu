@@ -40,8 +40,9 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c0, uint32_t c1, uint32_t
   out[3] = c[3];
 }
 
-// Uniform in the open interval (0, 1) from the top 24 bits.
-__device__ __forceinline__ float to_unit(uint32_t x) { return ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+// Uniform in the open interval (0, 1) from the top 23 bits: (k + 0.5) / 2^23
+// is exact in fp32 for every k < 2^23, so u never rounds to 0 or 1.
+__device__ __forceinline__ float to_unit(uint32_t x) { return ((float)(x >> 9) + 0.5f) * (1.0f / 8388608.0f); }
 
 struct Best {
   float v;
@@ -83,56 +84,65 @@ __device__ __forceinline__ Best block_argmax(Best b) {
   return b;
 }
 
+// Largest Gumbel value the generator can produce: u <= 1 - 2^-24, so
+// -log(-log(u)) <= -log(2^-24) = 24 ln 2 = 16.64 (plus margin for logf).
+constexpr float kGumbelMax = 16.7f;
+
+__device__ __forceinline__ float gumbel_at(uint64_t n, uint32_t seed) {
+  uint32_t r[4];
+  philox4x32_10((uint32_t)(n >> 2), (uint32_t)(n >> 34), seed, 0u, r);
+  return -logf(-logf(to_unit(r[n & 3])));
+}
+
 // Scores one row segment [0, n) whose column j has global index gcol0 + j in a
 // row of vocab_total columns; returns the (score, global index) maximum.
+// With T > 0 it runs two passes: (1) the largest logit and its lowest index
+// j*, giving the lower bound L = logit[j*] / T + g(j*) of the winning score;
+// (2) noise only for columns with logit / T >= L - kGumbelMax — every other
+// column's best possible score is below L, so skipping it cannot change the
+// result (exact, not an approximation).
 __device__ Best score_segment(const bf16* __restrict__ row, int n, int64_t gcol0, int64_t row_base, float temp,
                               uint32_t seed, bool vec) {
   Best best = {-INFINITY, INT64_MAX};
-  const float inv_t = temp > 0.f ? 1.f / temp : 0.f;
-  auto score = [&](float logit, int64_t gcol) {
-    if (temp > 0.f) {
-      const uint64_t n64 = (uint64_t)(row_base + gcol);
-      uint32_t r[4];
-      philox4x32_10((uint32_t)(n64 >> 2), (uint32_t)(n64 >> 34), seed, 0u, r);
-      const float u = to_unit(r[n64 & 3]);
-      return logit * inv_t - logf(-logf(u));
-    }
-    return logit;
-  };
-  if (vec) {
-    const int nv = n / 8;
-    for (int c = threadIdx.x; c < nv; c += kThreads) {
-      const uint4 raw = reinterpret_cast<const uint4*>(row)[c];
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      if (temp > 0.f) {
-        // columns gcol..gcol+7 share at most 3 Philox blocks
-        const int64_t g0 = gcol0 + c * 8;
-        const uint64_t n0 = (uint64_t)(row_base + g0);
-        uint32_t blk = 0xffffffffu, hi = 0, r[4] = {0, 0, 0, 0};
+  const int nv = vec ? n / 8 : 0;
+  // pass 1 (also the whole greedy path): largest logit, lowest index on ties
+  for (int c = threadIdx.x; c < nv; c += kThreads) {
+    const uint4 raw = reinterpret_cast<const uint4*>(row)[c];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint64_t nj = n0 + j;
-          if ((uint32_t)(nj >> 2) != blk || (uint32_t)(nj >> 34) != hi) {
-            blk = (uint32_t)(nj >> 2);
-            hi = (uint32_t)(nj >> 34);
-            philox4x32_10(blk, hi, seed, 0u, r);
-          }
-          const float2 p = __bfloat1622float2(h[j >> 1]);
-          const float logit = (j & 1) ? p.y : p.x;
-          take(best, logit * inv_t - logf(-logf(to_unit(r[nj & 3]))), g0 + j);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 p = __bfloat1622float2(h[j]);
-          take(best, p.x, gcol0 + c * 8 + 2 * j);
-          take(best, p.y, gcol0 + c * 8 + 2 * j + 1);
-        }
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 p = __bfloat1622float2(h[j]);
+      take(best, p.x, gcol0 + c * 8 + 2 * j);
+      take(best, p.y, gcol0 + c * 8 + 2 * j + 1);
     }
-    for (int j = nv * 8 + threadIdx.x; j < n; j += kThreads) take(best, score(__bfloat162float(row[j]), gcol0 + j), gcol0 + j);
-  } else {
-    for (int j = threadIdx.x; j < n; j += kThreads) take(best, score(__bfloat162float(row[j]), gcol0 + j), gcol0 + j);
+  }
+  for (int j = nv * 8 + threadIdx.x; j < n; j += kThreads) take(best, __bfloat162float(row[j]), gcol0 + j);
+  if (!(temp > 0.f)) return best;
+  const float inv_t = 1.f / temp;
+  best = block_argmax(best);
+  __shared__ float bound_s;
+  if (threadIdx.x == 0)
+    bound_s = best.i == INT64_MAX ? -INFINITY
+                                  : best.v * inv_t + gumbel_at((uint64_t)(row_base + best.i), seed) - kGumbelMax;
+  __syncthreads();
+  const float bound = bound_s;
+  best = {-INFINITY, INT64_MAX};
+  // pass 2: noise for the candidates only
+  for (int c = threadIdx.x; c < nv; c += kThreads) {
+    const uint4 raw = reinterpret_cast<const uint4*>(row)[c];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 p = __bfloat1622float2(h[j]);
+      const float l0 = p.x * inv_t, l1 = p.y * inv_t;
+      const int64_t g0 = gcol0 + c * 8 + 2 * j;
+      if (l0 >= bound) take(best, l0 + gumbel_at((uint64_t)(row_base + g0), seed), g0);
+      if (l1 >= bound) take(best, l1 + gumbel_at((uint64_t)(row_base + g0 + 1), seed), g0 + 1);
+    }
+  }
+  for (int j = nv * 8 + threadIdx.x; j < n; j += kThreads) {
+    const float l = __bfloat162float(row[j]) * inv_t;
+    if (l >= bound) take(best, l + gumbel_at((uint64_t)(row_base + gcol0 + j), seed), gcol0 + j);
   }
   return best;
 }

@@ -16,6 +16,7 @@ the decode graph at every TP size.
 """
 from __future__ import annotations
 
+import datetime
 import os
 import pickle
 from multiprocessing.shared_memory import SharedMemory
@@ -182,7 +183,8 @@ class ModelRunner:
         self.owns_process_group = False
         if not dist.is_initialized():
             dist.init_process_group("nccl", f"tcp://127.0.0.1:{config.rdzv_port}", world_size=self.world_size,
-                                    rank=rank, device_id=torch.device(f"cuda:{self._local_device(rank)}"))
+                                    rank=rank, device_id=torch.device(f"cuda:{self._local_device(rank)}"),
+                                    timeout=datetime.timedelta(seconds=300))
             self.owns_process_group = True
         if dist.get_world_size() != self.world_size:
             raise RuntimeError(f"process group has {dist.get_world_size()} ranks, config asks for {self.world_size}")

@@ -82,8 +82,14 @@ class TPAllReduce:
                   weight.data_ptr(), tokens, self.hidden, float(eps), mode, torch.cuda.current_stream().cuda_stream)
         return out, res_out
 
-    def close(self) -> None:
+    def close(self, group=None) -> None:
+        """Collective: every rank's kernels that read this rank's buffers must
+        be finished before the buffers are unmapped and freed."""
         if self.comm:
+            torch.cuda.synchronize(self.device)
+            if dist.is_initialized():
+                dist.barrier(group=group)
+                torch.cuda.synchronize(self.device)
             _lib.call("kvb_comm_destroy", self.comm)
             self.comm = ctypes.c_void_p()
             self.buffers = []

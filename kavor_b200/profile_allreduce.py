@@ -1,0 +1,116 @@
+"""All-reduce + residual add + RMSNorm microbenchmark over N GPUs of one node.
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        -m kavor_b200.profile_allreduce [--hidden 1024,4096,5120] [--tokens 1,16,256,4096,16384]
+
+For every (hidden, tokens) it times, on every rank with CUDA events around a
+CUDA graph of ``--iters`` calls (max over ranks), the fused NVLink kernel
+``kvb_allreduce_add_rmsnorm`` in its automatic, one-shot and two-shot modes,
+against the reference's sequence: NCCL ``all_reduce`` of the [T, H] bf16
+partial followed by the add+RMSNorm kernel. Inputs are x ~ N(0, 1) bf16,
+w ~ N(1, 0.1), eps 1e-6; consecutive calls alternate two partial buffers, as
+the layers of a forward do. Prints one JSON line per case on rank 0 with the
+average call time and the bus bandwidth 2 (N-1)/N T H 2 bytes / time.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from kavor_b200 import _kernels as K
+from kavor_b200 import _lib
+from kavor_b200.layers.allreduce import TPAllReduce
+
+
+def _time_graph(fn, iters: int, warmup: int) -> float:
+    """Seconds per call of ``fn`` (max over ranks), replayed from one CUDA graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(warmup):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3 / iters], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del g
+    torch.cuda.synchronize()
+    dist.barrier()
+    return float(t.item())
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--hidden", default="1024,4096,5120")
+    ap.add_argument("--tokens", default="1,16,256,4096,16384")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    hiddens = [int(x) for x in a.hidden.split(",")]
+    tokens = [int(x) for x in a.tokens.split(",")]
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    for H in hiddens:
+        tmax = max(tokens)
+        ar = TPAllReduce(tmax, H, dev)
+        w = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
+        for i in range(2):
+            ar.buffers[i].copy_(torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16))
+        nccl_x = [torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+        res = torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(tmax, H, device=dev, dtype=torch.bfloat16)
+        for T in tokens:
+            row = {"world": world, "hidden": H, "tokens": T, "bus_bytes": 2 * (world - 1) / world * T * H * 2}
+
+            def fused(mode):
+                def fn(i):
+                    _lib.call("kvb_allreduce_add_rmsnorm", ar.comm, i & 1, res.data_ptr(), res.data_ptr(),
+                              out.data_ptr(), w.data_ptr(), T, H, 1e-6, mode, torch.cuda.current_stream().cuda_stream)
+                return fn
+
+            for name, mode in (("fused_auto", 0), ("fused_one_shot", 1), ("fused_two_shot", 2)):
+                t = _time_graph(fused(mode), a.iters, a.warmup)
+                row[name + "_us"] = t * 1e6
+
+            def nccl(i):
+                x = nccl_x[i & 1][:T]
+                dist.all_reduce(x)
+                K.add_rmsnorm(x, res[:T], w, 1e-6, out=out[:T])
+
+            t = _time_graph(nccl, a.iters, a.warmup)
+            row["nccl_plus_add_rmsnorm_us"] = t * 1e6
+            row["fused_auto_busbw_gbs"] = row["bus_bytes"] / (row["fused_auto_us"] * 1e-6) / 1e9
+            row["nccl_busbw_gbs"] = row["bus_bytes"] / (t) / 1e9
+            row["device_error_bits"] = _lib.device_error(clear=True)
+            if rank == 0:
+                print(json.dumps(row), flush=True)
+        del nccl_x, res, out
+        ar.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

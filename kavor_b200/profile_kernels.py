@@ -6,10 +6,12 @@
     python -m kavor_b200.profile_kernels gemm --batch M --inter N --hidden K   (gemm_cublas: torch/cuBLAS)
 
 Allocates only the kernel's own inputs (a few hundred MB at most), runs
-``--warmup`` untimed launches, then ``--iters`` launches timed with CUDA events
-on the launching stream, rotating over ``--copies`` copies of the inputs so
-consecutive launches do not hit in L2, and prints one JSON line with the
-average launch time and the achieved algorithmic bandwidth.
+``--warmup`` untimed launches, then ``--iters`` launches captured in one CUDA
+graph and timed (one replay) with CUDA events on the launching stream — device
+time without host launch overhead (``--eager`` times plain launches instead) —
+rotating over ``--copies`` copies of the inputs so consecutive launches do not
+hit in L2 (use enough copies that they exceed the 126 MB L2), and prints one
+JSON line with the average launch time and the achieved algorithmic bandwidth.
 """
 from __future__ import annotations
 
@@ -144,6 +146,7 @@ def main(argv=None) -> int:
     ap.add_argument("--copies", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--eager", action="store_true", help="time eager launches (includes host overhead)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -152,10 +155,22 @@ def main(argv=None) -> int:
         run(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.iters):
-        run(i)
-    e1.record()
+    if a.eager:
+        e0.record()
+        for i in range(a.iters):
+            run(i)
+        e1.record()
+    else:
+        # launches captured once and replayed: device time only, no host overhead
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(a.iters):
+                run(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        graph.replay()
+        e1.record()
     torch.cuda.synchronize()
     t = e0.elapsed_time(e1) / 1e3 / a.iters
     res = {"kernel": a.kernel, "avg_launch_us": t * 1e6, "algorithmic_bytes": nbytes, "gbs": nbytes / t / 1e9}

@@ -180,7 +180,7 @@ def gumbel_scores(logits: torch.Tensor, temperatures: torch.Tensor, seed: int) -
     B, V = logits.shape
     n = np.arange(B * V, dtype=np.uint64)
     r = philox4x32_10(n >> np.uint64(2), seed)[np.arange(B * V), (n & np.uint64(3)).astype(np.int64)]
-    u = ((r >> 8).astype(np.float64) + 0.5) / 16777216.0
+    u = ((r >> 9).astype(np.float64) + 0.5) / 8388608.0
     g = torch.from_numpy(-np.log(-np.log(u))).view(B, V)
     t = temperatures.double().unsqueeze(1)
     return logits.double() / t + g

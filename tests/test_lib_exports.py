@@ -67,3 +67,27 @@ def test_ops_raise_without_a_cuda_tensor():
     x = torch.zeros(4, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         K.rmsnorm(x, torch.ones(128, dtype=torch.bfloat16), 1e-6)
+
+
+def test_gemm_plans_are_consistent(lib):
+    """Host-side GEMM planning (no launch): every plan covers the problem, fits
+    the SM budget (persistent) or forms whole clusters (split K), and needs no
+    scratch memory."""
+    import math
+
+    from kavor_b200 import _kernels as K
+
+    for M in (1, 7, 16, 64, 100, 256, 300, 2048, 16384):
+        for N, Kd in ((768, 4096), (6144, 4096), (4096, 512), (4096, 12288), (151936, 4096), (1000, 1024)):
+            p = K.gemm_plan(M, N, Kd)
+            assert p["mt"] in (16, 32, 64, 128, 256)
+            n_tiles, m_tiles = math.ceil(N / 128), math.ceil(M / p["mt"])
+            kb = math.ceil(Kd / 64)
+            assert 1 <= p["splits"] <= kb
+            assert p["units"] == n_tiles * m_tiles * p["splits"]
+            if p["splits"] == 1:  # persistent CTAs
+                assert 1 <= p["grid"] <= min(p["units"], 2 * 148)
+            else:  # one CTA per unit, clusters of `splits` CTAs along K, no empty part
+                assert p["splits"] in (2, 4, 8, 16) and p["grid"] == p["units"]
+                assert (p["splits"] - 1) * math.ceil(kb / p["splits"]) < kb
+            assert K.gemm_workspace_bytes(M, N, Kd) == 0  # the split reduces through distributed shared memory

@@ -1,0 +1,173 @@
+"""Tensor parallelism on 2 GPUs: the Qwen3 model sharded over two processes
+(dummy checkpoint through the TP weight loaders, fused NVLink all-reduce +
+add+RMSNorm, vocab-sharded sampling) against the CPU oracle on the full
+weights: logits cosine >= 0.999 and equal greedy tokens for a prefill and
+decode steps; and LLM.generate with tensor_parallel_size=2 (spawned worker,
+shared-memory mailbox) end to end."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, port, results):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "tests", "golden")]
+    import torch.distributed as dist
+
+    import cases
+    from kavor_b200.layers.allreduce import TPAllReduce, set_tp_allreduce
+    from kavor_b200.models import AutoModelForCausalLM
+    from kavor_b200.utils.context import reset_context, set_context
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=WORLD, rank=rank, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    out = {}
+    try:
+        cfg = cases.hf_config(cases.TINY)
+        torch.set_default_dtype(torch.bfloat16)
+        torch.set_default_device(dev)
+        model = AutoModelForCausalLM.model_class(cfg)(cfg)
+        torch.set_default_device("cpu")
+        torch.set_default_dtype(torch.float32)
+        ckpt = cases.checkpoint(cases.TINY, seed=5)
+        from kavor_b200.models import _assign
+
+        loaded = set()
+        for name, t in ckpt.items():
+            _assign(model, name, t.to(dev), model.packed_modules_mapping, loaded)
+        ar = TPAllReduce(1024, cfg.hidden_size, dev)
+        set_tp_allreduce(ar)
+        hkv = cfg.num_key_value_heads // WORLD
+        pools = [torch.zeros(8, 2, 256, hkv, 128, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        for lyr, pool in zip(model.model.layers, pools):
+            lyr.self_attn.attn.k_cache = [pool[:, 0]]
+            lyr.self_attn.attn.v_cache = [pool[:, 1]]
+        prompts = [[(13 * i + 7 * j) % 4000 + 3 for j in range(n)] for i, n in enumerate((37, 5, 100))]
+        tables = [[0], [3], [5]]
+        seqs = [list(p) for p in prompts]
+        i32 = dict(dtype=torch.int32, device=dev)
+        steps = []
+        with torch.inference_mode():
+            ids = torch.tensor([t for s in seqs for t in s], device=dev)
+            pos = torch.tensor([i for s in seqs for i in range(len(s))], device=dev)
+            cu = torch.tensor([0] + torch.tensor([len(s) for s in seqs]).cumsum(0).tolist(), **i32)
+            slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))], **i32)
+            for step in range(5):
+                if step == 0:
+                    set_context(True, cu, cu, max(map(len, seqs)), max(map(len, seqs)), slots)
+                else:
+                    set_context(False, slot_mapping=torch.tensor(
+                        [tables[b][0] * 256 + len(s) - 1 for b, s in enumerate(seqs)], **i32),
+                        context_lens=torch.tensor([len(s) for s in seqs], **i32),
+                        block_tables=torch.tensor(tables, **i32))
+                    ids = torch.tensor([s[-1] for s in seqs], device=dev)
+                    pos = torch.tensor([len(s) - 1 for s in seqs], device=dev)
+                hidden = model(ids, pos)
+                logits = model.compute_logits(hidden)  # gathered on rank 0
+                temps = torch.zeros(len(seqs), dtype=torch.float32, device=dev)
+                tok = model.lm_head.sample(hidden, temps, torch.zeros((), dtype=torch.int32, device=dev)).tolist()
+                reset_context()
+                steps.append((None if logits is None else logits.float().cpu(), tok))
+                for b, t in enumerate(tok):
+                    seqs[b].append(t)
+        out["steps"] = steps
+        out["prompts"] = prompts
+        set_tp_allreduce(None)
+        ar.close()
+    except Exception as e:
+        out["error"] = repr(e)
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    results[rank] = out
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_tp2_model_matches_oracle():
+    import torch.multiprocessing as mp
+
+    import cases
+    from oracle import model as omodel
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _port()
+        ps = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(WORLD)]
+        for p in ps:
+            p.start()
+        for p in ps:
+            p.join(timeout=600)
+        for p in ps:
+            if p.is_alive():
+                p.kill()
+        res = dict(results)
+    assert "error" not in res[0] and "error" not in res[1], res
+    steps0, steps1 = res[0]["steps"], res[1]["steps"]
+    # every rank agrees on the sampled tokens
+    assert [t for _, t in steps0] == [t for _, t in steps1]
+    # oracle on the full (TP=1) weights, same token stream
+    shape = omodel.Shape(hidden=512, inter=1024, layers=2, hq=4, hkv=2, vocab=4096)
+    p = cases.checkpoint(cases.TINY, seed=5)
+    kv = [(torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16), torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16))
+          for _ in range(2)]
+    seqs = [list(x) for x in res[0]["prompts"]]
+    tables = [[0], [3], [5]]
+    for step, (logits, tok) in enumerate(steps0):
+        if step == 0:
+            ids = torch.tensor([t for s in seqs for t in s])
+            pos = torch.tensor([i for s in seqs for i in range(len(s))])
+            cu = torch.tensor([0] + torch.tensor([len(s) for s in seqs]).cumsum(0).tolist(), dtype=torch.int32)
+            slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))])
+            batch = omodel.Batch(True, pos, slots, cu, cu)
+        else:
+            ids = torch.tensor([s[-1] for s in seqs])
+            pos = torch.tensor([len(s) - 1 for s in seqs])
+            slots = torch.tensor([tables[b][0] * 256 + len(s) - 1 for b, s in enumerate(seqs)])
+            batch = omodel.Batch(False, pos, slots, context_lens=torch.tensor([len(s) for s in seqs], dtype=torch.int32),
+                                 block_tables=torch.tensor(tables, dtype=torch.int32))
+        _, ref = omodel.forward(p, ids, batch, kv, shape)
+        cos = torch.nn.functional.cosine_similarity(logits, ref.float(), dim=-1)
+        assert cos.min().item() >= 0.999, (step, cos)
+        assert tok == ref.float().argmax(-1).tolist(), step
+        for b, t in enumerate(tok):
+            seqs[b].append(t)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_llm_generate_tp2(tmp_path):
+    import torch.distributed as dist
+
+    from kavor_b200 import LLM, SamplingParams
+    from kavor_b200.config import write_model_dir
+
+    if dist.is_initialized():
+        dist.destroy_process_group()
+    d = write_model_dir(str(tmp_path / "m"), "Qwen3-0.6B", num_hidden_layers=2, vocab_size=4096,
+                        max_position_embeddings=4096)
+    llm = LLM(d, load_format="dummy", tensor_parallel_size=2, max_model_len=1024, max_num_seqs=8,
+              max_num_batched_tokens=1024, num_kvcache_blocks=32, rdzv_port=_port())
+    try:
+        prompts = [[(3 * j + i) % 4000 + 1 for j in range(50 + 30 * i)] for i in range(4)]
+        out = llm.generate(prompts, SamplingParams(temperature=0.8, max_tokens=12, ignore_eos=True), use_tqdm=False)
+        assert [len(o["token_ids"]) for o in out] == [12] * 4
+        assert all(0 <= t < 4096 for o in out for t in o["token_ids"])
+    finally:
+        llm.exit()

@@ -223,6 +223,19 @@ int kvb_comm_open_peers(void* comm, const void* handles);
 int kvb_comm_data_buffer(void* comm, int index, void** ptr, size_t* bytes);
 int kvb_comm_destroy(void* comm);
 
+/* Alternative to kvb_comm_create/open_peers: attach to a symmetric area the
+ * caller allocated and mapped on every rank (e.g. torch symmetric memory),
+ * at least kvb_comm_area_size(max_bytes) bytes, zero-filled on every rank
+ * before the first call. peer_bases[p] = rank p's area as mapped in this
+ * process (256-byte aligned); multicast_base = the area's NVLink multicast
+ * (NVLS) mapping, or 0 when the system has none. The area stays owned by the
+ * caller; kvb_comm_destroy frees only the library's own counters. */
+int kvb_comm_area_size(size_t max_bytes, size_t* bytes);
+int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t multicast_base, size_t area_bytes,
+                    size_t max_bytes, void** comm);
+/* 1 when the communicator has a multicast mapping (switch-reduced modes). */
+int kvb_comm_has_multicast(void* comm);
+
 /* Fused all-reduce + residual add + RMSNorm over the TP group
  * (linear.py:156-160 followed by layernorm.py:114-140; with residual_in =
  * NULL the embedding all-reduce followed by qwen3.py:155-156):
@@ -230,8 +243,12 @@ int kvb_comm_destroy(void* comm);
  *   r = fp32(y) + fp32(residual_in) (or y), residual_out <- bf16(r),
  *   out = bf16(bf16(r * rsqrt(mean(r^2) + eps)) * weight).
  * Every rank of the group must make the same calls in the same order. mode:
- * 0 automatic, 1 one-shot (every rank reduces every row), 2 two-shot (each
- * rank reduces 1/N of the rows, then exchanges results). Peer waits are
+ * 0 automatic, 1 one-shot (every rank reduces every row from the peers'
+ * buffers), 2 two-shot (each rank reduces 1/N of the rows, then exchanges
+ * results), 3 one-shot through the NVLink switch (multimem.ld_reduce, fp32
+ * accumulation), 4 two-shot through the switch (reduce 1/N of the rows, then
+ * multimem.st them to every rank); 3 and 4 need a multicast mapping
+ * (kvb_comm_attach). Peer waits are
  * bounded (~1 s); on expiry the kernel raises device error bit 16 and returns.
  * residual_out may alias residual_in. Consecutive calls must use different
  * data buffers. */

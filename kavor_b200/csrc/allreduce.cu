@@ -48,8 +48,10 @@ struct Comm {
   size_t data_bytes = 0;   // capacity of one data buffer (bytes)
   uint8_t* base = nullptr;  // local symmetric allocation
   uint8_t* peer[kMaxRanks] = {};
+  uint8_t* mc = nullptr;    // NVLink multicast mapping of the area (NULL: none)
   uint32_t* counters = nullptr;
   bool opened[kMaxRanks] = {};
+  bool owns_area = true;    // false: the area was attached (allocated and mapped by the caller)
 };
 
 struct Layout {
@@ -80,7 +82,9 @@ struct ArArgs {
   bf16* residual_out;
   bf16* out;
   const bf16* weight;
-  int rank, world, tokens, hidden, two_shot;
+  const bf16* mc_data;            // multicast address of this call's partial buffer (NVLS modes)
+  bf16* mc_result;                // multicast address of the result area (NVLS two-shot)
+  int rank, world, tokens, hidden, two_shot, nvls;
   size_t result_stride;           // elements between the out rows and residual rows of a result area
   float eps;
 };
@@ -89,8 +93,27 @@ struct alignas(16) Vec8 {
   __nv_bfloat162 h[4];
 };
 
-__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// NVLink SHARP: one 16-byte load that returns the sum over every rank's copy
+// (reduced in the switch, fp32 accumulation, one bf16 rounding), and one
+// 16-byte store that lands in every rank's copy.
+__device__ __forceinline__ Vec8 mc_ld_reduce(const bf16* mc) {
+  Vec8 v;
+  uint32_t* r = reinterpret_cast<uint32_t*>(&v);
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_store(bf16* mc, const Vec8& v) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(&v);
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   uint32_t v;
@@ -98,16 +121,23 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   return v;
 }
 
-// Flag round: returns false if a peer did not arrive within the spin budget.
-__device__ bool flag_round(const ArArgs& a, int phase, uint32_t v, int* ok_s) {
+// Flag round: block b tells every rank "my part of call v is ready" and waits
+// until every rank told it the same. Returns false if a peer did not arrive
+// within the spin budget. `publish` = this kernel wrote the data the peers
+// will read (two-shot results): a system-scope release fence orders the
+// block's writes (all threads, via the preceding __syncthreads) before the
+// flag. The partial sums of the first round were written by earlier kernels,
+// which completed before this one started, so that round needs no fence.
+template <int W>
+__device__ bool flag_round(const ArArgs& a, int phase, uint32_t v, bool publish, int* ok_s) {
   const int b = blockIdx.x;
-  if (threadIdx.x < a.world) {
-    __threadfence_system();
-    st_release(a.flags[threadIdx.x] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + a.rank, v);
+  if (threadIdx.x < W) {
+    if (publish) asm volatile("fence.acq_rel.sys;" ::: "memory");
+    st_relaxed_sys(a.flags[threadIdx.x] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + a.rank, v);
   }
   if (threadIdx.x == 0) *ok_s = 1;
   __syncthreads();
-  if (threadIdx.x < a.world) {
+  if (threadIdx.x < W) {
     const uint32_t* f = a.flags[a.rank] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + threadIdx.x;
     if (ld_acquire(f) != v) {
       const long long t0 = clock64();
@@ -151,51 +181,115 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-// Reduce row t over all ranks, add the residual, normalise; writes the bf16
-// residual and output rows to (res_dst, out_dst).
+// Reduce row t over the W ranks, add the residual, normalise; writes the bf16
+// residual and output rows to (res_dst, out_dst). Thread j owns the 16-byte
+// chunks j, j + 256, ... (NCH of them); the loads of G chunks x W ranks (8
+// vectors) are all issued before any is used, so a row costs one NVLink round
+// trip per group instead of one per (chunk, rank). MC: the sum comes from the
+// switch (one multicast load per chunk); ST_MC: the rows are stored through the
+// multicast mapping into every rank's result area.
+template <int W, int NCH, bool MC, bool ST_MC>
 __device__ void reduce_row(const ArArgs& a, int t, bf16* out_dst, bf16* res_dst, float* red) {
+  constexpr int WL = MC ? 1 : W;  // vectors loaded per chunk
+  constexpr int G = (8 / WL) < NCH ? (8 / WL) : NCH;
   const int nch = a.hidden / 8;
   const int64_t row = (int64_t)t * a.hidden;
-  float v[kMaxChunks][8];
+  float v[NCH][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    if (c < nch) {
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int p = 0; p < a.world; ++p) {
-        float f[8];
-        unpack8(reinterpret_cast<const Vec8*>(a.data[p] + row)[c], f);
+  for (int g0 = 0; g0 < NCH; g0 += G) {
+    Vec8 in[G][WL];
+    Vec8 rin[G];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    for (int i = 0; i < G; ++i) {
+      const int c = threadIdx.x + (g0 + i) * kThreads;
+      if (g0 + i < NCH && c < nch) {
+        if constexpr (MC) {
+          in[i][0] = mc_ld_reduce(a.mc_data + row + (int64_t)c * 8);
+        } else {
+#pragma unroll
+          for (int p = 0; p < W; ++p) in[i][p] = reinterpret_cast<const Vec8*>(a.data[p] + row)[c];
+        }
+        if (a.residual_in) rin[i] = reinterpret_cast<const Vec8*>(a.residual_in + row)[c];
       }
-      float r[8];
-      if (a.residual_in) unpack8(reinterpret_cast<const Vec8*>(a.residual_in + row)[c], r);
+    }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float y = bf16_round(acc[j]);  // the all-reduce result is a bf16 tensor in the reference
-        v[i][j] = a.residual_in ? y + r[j] : y;
-        ss += v[i][j] * v[i][j];
+    for (int i = 0; i < G; ++i) {
+      const int c = threadIdx.x + (g0 + i) * kThreads;
+      if (g0 + i < NCH && c < nch) {
+        float acc[8], f[8];
+        unpack8(in[i][0], acc);
+#pragma unroll
+        for (int p = 1; p < WL; ++p) {  // rank order: identical sums on every rank
+          unpack8(in[i][p], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += f[j];
+        }
+        float r[8];
+        if (a.residual_in) unpack8(rin[i], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float y = bf16_round(acc[j]);  // the all-reduce result is a bf16 tensor in the reference
+          v[g0 + i][j] = a.residual_in ? y + r[j] : y;
+          ss += v[g0 + i][j] * v[g0 + i][j];
+        }
       }
     }
   }
   const float rstd = rsqrtf(block_sum(ss, red) / (float)a.hidden + a.eps);
   const Vec8* w = reinterpret_cast<const Vec8*>(a.weight);
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
+  for (int i = 0; i < NCH; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < nch) {
       float wf[8], y[8];
       unpack8(w[c], wf);
-      reinterpret_cast<Vec8*>(res_dst)[c] = pack8(v[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) y[j] = bf16_round(v[i][j] * rstd) * wf[j];
-      reinterpret_cast<Vec8*>(out_dst)[c] = pack8(y);
+      if constexpr (ST_MC) {
+        mc_store(res_dst + (int64_t)c * 8, pack8(v[i]));
+        mc_store(out_dst + (int64_t)c * 8, pack8(y));
+      } else {
+        reinterpret_cast<Vec8*>(res_dst)[c] = pack8(v[i]);
+        reinterpret_cast<Vec8*>(out_dst)[c] = pack8(y);
+      }
     }
   }
 }
 
-__global__ void __launch_bounds__(kThreads) ar_add_rmsnorm_kernel(const __grid_constant__ ArArgs a) {
+// Rows t = blockIdx.x, blockIdx.x + gridDim.x, ... of the two-shot result
+// area `src` (out rows, then residual rows `result_stride` further) -> out,
+// residual_out.
+template <int NCH>
+__device__ void copy_rows(const ArArgs& a, int t, const bf16* src) {
+  const int nch = a.hidden / 8;
+  const Vec8* so = reinterpret_cast<const Vec8*>(src);
+  const Vec8* sr = reinterpret_cast<const Vec8*>(src + a.result_stride);
+  Vec8* doo = reinterpret_cast<Vec8*>(a.out + (int64_t)t * a.hidden);
+  Vec8* dr = reinterpret_cast<Vec8*>(a.residual_out + (int64_t)t * a.hidden);
+  Vec8 bo[NCH], br[NCH];
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c = threadIdx.x + i * kThreads;
+    if (c < nch) {
+      bo[i] = so[c];
+      br[i] = sr[c];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c = threadIdx.x + i * kThreads;
+    if (c < nch) {
+      doo[c] = bo[i];
+      dr[c] = br[i];
+    }
+  }
+}
+
+// Two blocks per SM at most 128 registers: every block of a call (<= 256) is
+// resident at once, so no block can wait on a peer block that is not running.
+template <int W, int NCH>
+__global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __grid_constant__ ArArgs a) {
   __shared__ float red[kThreads / 32];
   __shared__ uint32_t v_s;
   __shared__ int ok_s;
@@ -205,34 +299,51 @@ __global__ void __launch_bounds__(kThreads) ar_add_rmsnorm_kernel(const __grid_c
   }
   __syncthreads();
   const uint32_t v = v_s;
-  if (!flag_round(a, 0, v, &ok_s)) return;
+  if (!flag_round<W>(a, 0, v, false, &ok_s)) return;
   const int nb = gridDim.x;
-  if (!a.two_shot) {
+  const int64_t H = a.hidden;
+  if (a.nvls == 1) {  // every rank reduces every row through the switch
     for (int t = blockIdx.x; t < a.tokens; t += nb)
-      reduce_row(a, t, a.out + (int64_t)t * a.hidden, a.residual_out + (int64_t)t * a.hidden, red);
+      reduce_row<W, NCH, true, false>(a, t, a.out + t * H, a.residual_out + t * H, red);
     return;
   }
-  // two-shot: rows t with t % world == rank are reduced here and published
+  if (a.nvls == 2) {  // rank r reduces rows t % W == r through the switch and multicasts them
+    for (int t = blockIdx.x; t < a.tokens; t += nb) {
+      if (t % W != a.rank) continue;
+      bf16* o = a.mc_result + t * H;
+      reduce_row<W, NCH, true, true>(a, t, o, o + a.result_stride, red);
+    }
+    __syncthreads();
+    if (!flag_round<W>(a, 1, v, true, &ok_s)) return;
+    for (int t = blockIdx.x; t < a.tokens; t += nb) copy_rows<NCH>(a, t, a.result[a.rank] + t * H);
+    return;
+  }
+  if (!a.two_shot) {
+    for (int t = blockIdx.x; t < a.tokens; t += nb)
+      reduce_row<W, NCH, false, false>(a, t, a.out + t * H, a.residual_out + t * H, red);
+    return;
+  }
+  // two-shot over peer memory: rows t with t % W == rank are reduced here and
+  // published, then every rank copies every row from its owner
   bf16* mine = a.result[a.rank];
   for (int t = blockIdx.x; t < a.tokens; t += nb) {
-    if (t % a.world != a.rank) continue;
-    bf16* o = mine + (int64_t)t * a.hidden;
-    reduce_row(a, t, o, o + a.result_stride, red);
-    __syncthreads();
+    if (t % W != a.rank) continue;
+    bf16* o = mine + t * H;
+    reduce_row<W, NCH, false, false>(a, t, o, o + a.result_stride, red);
   }
-  if (!flag_round(a, 1, v, &ok_s)) return;
-  const int nch = a.hidden / 8;
-  for (int t = blockIdx.x; t < a.tokens; t += nb) {
-    const bf16* src = a.result[t % a.world] + (int64_t)t * a.hidden;
-    const Vec8* so = reinterpret_cast<const Vec8*>(src);
-    const Vec8* sr = reinterpret_cast<const Vec8*>(src + a.result_stride);
-    Vec8* doo = reinterpret_cast<Vec8*>(a.out + (int64_t)t * a.hidden);
-    Vec8* dr = reinterpret_cast<Vec8*>(a.residual_out + (int64_t)t * a.hidden);
-    for (int c = threadIdx.x; c < nch; c += kThreads) {
-      doo[c] = so[c];
-      dr[c] = sr[c];
-    }
-  }
+  __syncthreads();
+  if (!flag_round<W>(a, 1, v, true, &ok_s)) return;
+  for (int t = blockIdx.x; t < a.tokens; t += nb) copy_rows<NCH>(a, t, a.result[t % W] + t * H);
+}
+
+template <int W>
+cudaError_t launch_w(const ArArgs& a, int blocks, int nch, cudaStream_t st) {
+  const int per = (nch + kThreads - 1) / kThreads;
+  if (per <= 1) ar_add_rmsnorm_kernel<W, 1><<<blocks, kThreads, 0, st>>>(a);
+  else if (per <= 2) ar_add_rmsnorm_kernel<W, 2><<<blocks, kThreads, 0, st>>>(a);
+  else if (per <= 4) ar_add_rmsnorm_kernel<W, 4><<<blocks, kThreads, 0, st>>>(a);
+  else ar_add_rmsnorm_kernel<W, 8><<<blocks, kThreads, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -243,8 +354,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 using namespace kvb;
 
 extern "C" int kvb_comm_create(int rank, int world, size_t max_bytes, void** comm, void* ipc_handle) {
-  if (!comm || !ipc_handle || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || max_bytes == 0)
-    return set_error(kInvalid, "kvb_comm_create: bad arguments (world must be 1..8)");
+  if (!comm || !ipc_handle || rank < 0 || rank >= world || max_bytes == 0)
+    return set_error(kInvalid, "kvb_comm_create: bad arguments");
+  if (world != 1 && world != 2 && world != 4 && world != 8)
+    return set_error(kUnsupported, "kvb_comm_create: world size must be 1, 2, 4 or 8 (got %d)", world);
   Comm* c = new Comm();
   c->rank = rank;
   c->world = world;
@@ -305,18 +418,64 @@ extern "C" int kvb_comm_destroy(void* comm) {
   if (e != cudaSuccess) rc = cuda_status(e, "kvb_comm_destroy: synchronize");
   for (int p = 0; p < c->world; ++p)
     if (c->opened[p]) cudaIpcCloseMemHandle(c->peer[p]);
-  cudaFree(c->base);
+  if (c->owns_area) cudaFree(c->base);
   cudaFree(c->counters);
   delete c;
   return rc;
+}
+
+extern "C" int kvb_comm_area_size(size_t max_bytes, size_t* bytes) {
+  if (!bytes || max_bytes == 0) return set_error(kInvalid, "kvb_comm_area_size: bad arguments");
+  *bytes = layout_of(max_bytes).total;
+  return kOk;
+}
+
+extern "C" int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t multicast_base,
+                               size_t area_bytes, size_t max_bytes, void** comm) {
+  if (!comm || !peer_bases || rank < 0 || rank >= world || max_bytes == 0)
+    return set_error(kInvalid, "kvb_comm_attach: bad arguments");
+  if (world != 1 && world != 2 && world != 4 && world != 8)
+    return set_error(kUnsupported, "kvb_comm_attach: world size must be 1, 2, 4 or 8 (got %d)", world);
+  const Layout L = layout_of(max_bytes);
+  if (area_bytes < L.total)
+    return set_error(kInvalid, "kvb_comm_attach: area of %zu bytes, %zu needed", area_bytes, L.total);
+  for (int p = 0; p < world; ++p)
+    if (!peer_bases[p] || (peer_bases[p] & 255)) return set_error(kInvalid, "kvb_comm_attach: peer %d base NULL or unaligned", p);
+  if (multicast_base & 255) return set_error(kInvalid, "kvb_comm_attach: multicast base unaligned");
+  Comm* c = new Comm();
+  c->rank = rank;
+  c->world = world;
+  c->data_bytes = max_bytes;
+  c->owns_area = false;
+  c->base = reinterpret_cast<uint8_t*>(peer_bases[rank]);
+  for (int p = 0; p < world; ++p) c->peer[p] = reinterpret_cast<uint8_t*>(peer_bases[p]);
+  c->mc = reinterpret_cast<uint8_t*>(multicast_base);
+  cudaError_t e = cudaGetDevice(&c->device);
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (c->counters) cudaFree(c->counters);
+    delete c;
+    return cuda_status(e, "kvb_comm_attach");
+  }
+  *comm = c;
+  return kOk;
+}
+
+extern "C" int kvb_comm_has_multicast(void* comm) {
+  Comm* c = static_cast<Comm*>(comm);
+  return c && c->mc ? 1 : 0;
 }
 
 extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void* residual_in, void* residual_out,
                                          void* out, const void* weight, int tokens, int hidden, float eps,
                                          int mode, void* stream) {
   Comm* c = static_cast<Comm*>(comm);
-  if (!c || data_index < 0 || data_index >= kNumData || tokens < 0 || hidden <= 0 || mode < 0 || mode > 2)
+  if (!c || data_index < 0 || data_index >= kNumData || tokens < 0 || hidden <= 0 || mode < 0 || mode > 4)
     return set_error(kInvalid, "kvb_allreduce_add_rmsnorm: bad arguments");
+  if (mode >= 3 && !c->mc)
+    return set_error(kUnsupported, "kvb_allreduce_add_rmsnorm: mode %d needs an NVLink multicast mapping", mode);
   if (tokens == 0) return kOk;
   if (!residual_out || !out || !weight) return set_error(kInvalid, "kvb_allreduce_add_rmsnorm: NULL pointer");
   if (hidden % 8 || hidden > kThreads * kMaxChunks * 8 || !aligned16(out) || !aligned16(residual_out) ||
@@ -343,11 +502,29 @@ extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void*
   a.world = c->world;
   a.tokens = tokens;
   a.hidden = hidden;
-  // mode 0: automatic (one-shot up to 512 KiB per rank), 1: one-shot, 2: two-shot
-  a.two_shot = c->world > 1 && (mode == 2 || (mode == 0 && bytes > (512u << 10)));
+  // mode 0: automatic, 1/2: one-/two-shot over peer memory, 3/4: one-/two-shot
+  // through the NVLink switch (multicast). Peer one-shot reads (world - 1)
+  // full partials per rank, peer two-shot 2 (world - 1) / world of them plus a
+  // second flag round; switch one-shot reads one reduced copy, switch
+  // two-shot 1/world of it and multicasts 2/world back.
+  a.two_shot = c->world > 2 && (mode == 2 || (mode == 0 && bytes * c->world > (8u << 20)));
+  if (mode == 2 && c->world > 1) a.two_shot = 1;
+  a.nvls = 0;
+  if (mode == 3 || mode == 4) a.nvls = mode - 2;
+  if (mode == 0 && c->mc && c->world > 2) a.nvls = (size_t)tokens >= (size_t)c->world * 8 ? 2 : 1;
+  a.mc_data = c->mc ? reinterpret_cast<const bf16*>(c->mc + L.data[data_index]) : nullptr;
+  a.mc_result = c->mc ? reinterpret_cast<bf16*>(c->mc + L.result) : nullptr;
   a.result_stride = ((c->data_bytes + 255) & ~size_t(255)) / 2;
   a.eps = eps;
   const int blocks = tokens < kMaxBlocks ? tokens : kMaxBlocks;
-  ar_add_rmsnorm_kernel<<<blocks, kThreads, 0, (cudaStream_t)stream>>>(a);
-  return cuda_status(cudaGetLastError(), "kvb_allreduce_add_rmsnorm launch");
+  const int nch = hidden / 8;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  switch (c->world) {
+    case 1: e = launch_w<1>(a, blocks, nch, st); break;
+    case 2: e = launch_w<2>(a, blocks, nch, st); break;
+    case 4: e = launch_w<4>(a, blocks, nch, st); break;
+    default: e = launch_w<8>(a, blocks, nch, st); break;
+  }
+  return cuda_status(e, "kvb_allreduce_add_rmsnorm launch");
 }

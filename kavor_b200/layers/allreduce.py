@@ -3,10 +3,11 @@
 Replaces, for TP > 1, the NCCL all-reduce after every row-parallel projection
 and the vocab-parallel embedding (linear.py:158-159, embed_head.py:39-41)
 together with the add+RMSNorm that always follows it in Qwen3
-(qwen3.py:155-160, 185). Each rank owns a symmetric area allocated by the
-library (``kvb_comm_create``); the CUDA IPC handles are exchanged once over
-the existing process group, after which every call is a single kernel that
-reads the peers' partial sums directly over NVLink.
+(qwen3.py:155-160, 185). Each rank owns a symmetric area: mapped by torch
+symmetric memory (peer pointers, and an NVLink multicast mapping where the
+NVSwitch offers one, for sums reduced in the switch), or allocated by the
+library with its CUDA IPC handles exchanged over the process group. Every call
+is then a single kernel that reads the peers' partial sums over NVLink.
 
 The producing kernel (row-parallel GEMM or embedding) writes its rank-local
 result straight into one of three data buffers of the symmetric area
@@ -32,24 +33,44 @@ class _CudaArray:
 
 
 class TPAllReduce:
+    """backend: "symmetric" maps the area with torch symmetric memory (peer
+    pointers plus, where the NVSwitch supports it, an NVLink multicast mapping
+    for the switch-reduced modes); "ipc" lets the library allocate it and
+    exchanges CUDA IPC handles; "auto" tries symmetric first."""
 
     EMBED_BUFFER = 2
 
-    def __init__(self, max_tokens: int, hidden: int, device: torch.device, group=None):
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device, group=None, backend: str = "auto",
+                 mode: int = 0):
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.hidden = hidden
         self.max_tokens = max_tokens
         self.device = device
-        lib = _lib.load()
-        hs = lib.kvb_comm_ipc_handle_size()
-        handle = (ctypes.c_ubyte * hs)()
+        self.mode = mode
         self.comm = ctypes.c_void_p()
-        _lib.call("kvb_comm_create", self.rank, self.world, max_tokens * hidden * 2, ctypes.byref(self.comm), handle)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        blob = b"".join(handles)
-        _lib.call("kvb_comm_open_peers", self.comm, ctypes.c_char_p(blob))
+        self._symm = None
+        self.backend = None
+        max_bytes = max_tokens * hidden * 2
+        if backend in ("auto", "symmetric"):
+            ok = 1
+            try:
+                self._attach_symmetric(max_bytes, group)
+            except Exception as e:  # noqa: BLE001 - fall back to the library's own IPC mapping
+                if backend == "symmetric":
+                    raise
+                self._symm_error = repr(e)
+                ok = 0
+            # every rank must take the same path
+            flag = torch.tensor([ok], dtype=torch.int32, device=device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+            if not int(flag.item()) and self.comm:
+                _lib.call("kvb_comm_destroy", self.comm)
+                self.comm = ctypes.c_void_p()
+                self._symm = None
+        if not self.comm:
+            self._create_ipc(max_bytes, group)
+        self.multicast = bool(_lib.load().kvb_comm_has_multicast(self.comm))
         self.buffers = []
         for i in range(3):
             ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
@@ -58,6 +79,33 @@ class TPAllReduce:
             self.buffers.append(raw.view(torch.bfloat16).view(max_tokens, hidden))
         dist.barrier(group=group)
         self._next = 0
+
+    def _create_ipc(self, max_bytes: int, group) -> None:
+        lib = _lib.load()
+        hs = lib.kvb_comm_ipc_handle_size()
+        handle = (ctypes.c_ubyte * hs)()
+        _lib.call("kvb_comm_create", self.rank, self.world, max_bytes, ctypes.byref(self.comm), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        _lib.call("kvb_comm_open_peers", self.comm, ctypes.c_char_p(b"".join(handles)))
+        self.backend = "ipc"
+
+    def _attach_symmetric(self, max_bytes: int, group) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        n = ctypes.c_size_t()
+        _lib.call("kvb_comm_area_size", max_bytes, ctypes.byref(n))
+        area = symm_mem.empty(int(n.value), dtype=torch.uint8, device=self.device)
+        area.zero_()
+        handle = symm_mem.rendezvous(area, group if group is not None else dist.group.WORLD)
+        ptrs = [int(p) for p in handle.buffer_ptrs]
+        mc = int(handle.multicast_ptr) if getattr(handle, "multicast_ptr", 0) else 0
+        arr = (ctypes.c_uint64 * self.world)(*ptrs)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+        _lib.call("kvb_comm_attach", self.rank, self.world, arr, mc, int(n.value), max_bytes, ctypes.byref(self.comm))
+        self._symm = (area, handle)
+        self.backend = "symmetric+multicast" if mc else "symmetric"
 
     def start_forward(self) -> None:
         self._next = 0
@@ -79,7 +127,8 @@ class TPAllReduce:
         res_out = residual if residual is not None else torch.empty_like(out)
         _lib.call("kvb_allreduce_add_rmsnorm", self.comm, index,
                   residual.data_ptr() if residual is not None else None, res_out.data_ptr(), out.data_ptr(),
-                  weight.data_ptr(), tokens, self.hidden, float(eps), mode, torch.cuda.current_stream().cuda_stream)
+                  weight.data_ptr(), tokens, self.hidden, float(eps), mode or self.mode,
+                  torch.cuda.current_stream().cuda_stream)
         return out, res_out
 
     def close(self, group=None) -> None:
@@ -93,6 +142,7 @@ class TPAllReduce:
             _lib.call("kvb_comm_destroy", self.comm)
             self.comm = ctypes.c_void_p()
             self.buffers = []
+            self._symm = None
 
 
 _TP: TPAllReduce | None = None

@@ -5,9 +5,10 @@
 
 For every (hidden, tokens) it times, on every rank with CUDA events around a
 CUDA graph of ``--iters`` calls (max over ranks), the fused NVLink kernel
-``kvb_allreduce_add_rmsnorm`` in its automatic, one-shot and two-shot modes,
-against the reference's sequence: NCCL ``all_reduce`` of the [T, H] bf16
-partial followed by the add+RMSNorm kernel. Inputs are x ~ N(0, 1) bf16,
+``kvb_allreduce_add_rmsnorm`` in its automatic mode and each explicit mode
+(peer one-shot / two-shot; switch-reduced one-shot / two-shot when the area has
+an NVLink multicast mapping), against the reference's sequence: NCCL
+``all_reduce`` of the [T, H] bf16 partial followed by the add+RMSNorm kernel. Inputs are x ~ N(0, 1) bf16,
 w ~ N(1, 0.1), eps 1e-6; consecutive calls alternate two partial buffers, as
 the layers of a forward do. Prints one JSON line per case on rank 0 with the
 average call time and the bus bandwidth 2 (N-1)/N T H 2 bytes / time.
@@ -62,6 +63,7 @@ def main(argv=None) -> int:
     ap.add_argument("--tokens", default="1,16,256,4096,16384")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--backend", default="auto", choices=["auto", "symmetric", "ipc"])
     a = ap.parse_args(argv)
     hiddens = [int(x) for x in a.hidden.split(",")]
     tokens = [int(x) for x in a.tokens.split(",")]
@@ -73,7 +75,10 @@ def main(argv=None) -> int:
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     for H in hiddens:
         tmax = max(tokens)
-        ar = TPAllReduce(tmax, H, dev)
+        ar = TPAllReduce(tmax, H, dev, backend=a.backend)
+        modes = (("fused_auto", 0), ("fused_one_shot", 1), ("fused_two_shot", 2))
+        if ar.multicast:
+            modes += (("fused_switch_one_shot", 3), ("fused_switch_two_shot", 4))
         w = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
         for i in range(2):
             ar.buffers[i].copy_(torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16))
@@ -81,7 +86,8 @@ def main(argv=None) -> int:
         res = torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16)
         out = torch.empty(tmax, H, device=dev, dtype=torch.bfloat16)
         for T in tokens:
-            row = {"world": world, "hidden": H, "tokens": T, "bus_bytes": 2 * (world - 1) / world * T * H * 2}
+            row = {"world": world, "hidden": H, "tokens": T, "backend": ar.backend,
+                   "bus_bytes": 2 * (world - 1) / world * T * H * 2}
 
             def fused(mode):
                 def fn(i):
@@ -89,7 +95,7 @@ def main(argv=None) -> int:
                               out.data_ptr(), w.data_ptr(), T, H, 1e-6, mode, torch.cuda.current_stream().cuda_stream)
                 return fn
 
-            for name, mode in (("fused_auto", 0), ("fused_one_shot", 1), ("fused_two_shot", 2)):
+            for name, mode in modes:
                 t = _time_graph(fused(mode), a.iters, a.warmup)
                 row[name + "_us"] = t * 1e6
 

@@ -339,16 +339,28 @@ def run_ours(args) -> int:
         a = attn[i % len(attn)]
         K.paged_decode_attention(q, a.k_cache[0], a.v_cache[0], bt, cl, 128 ** -0.5, out=out)
 
-    for i in range(3):
-        attn_launch(i)
-    torch.cuda.synchronize()
+    # launches captured in one CUDA graph and replayed, so the figure is device
+    # time (eager launches of a ~20 us kernel would time the host instead)
     n_attn = 2 * len(attn)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(3):
+            attn_launch(i)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    attn_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(attn_graph):
+        for i in range(n_attn):
+            attn_launch(i)
+    attn_graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(n_attn):
-        attn_launch(i)
+    attn_graph.replay()
     e1.record()
     torch.cuda.synchronize()
+    del attn_graph
     t_attn = max_over_ranks(e0.elapsed_time(e1) / 1e3 / n_attn)
     ctx_now = int(cl[0].item())
     a_bytes = attention_bytes(B, ctx_now, hq, hkv)

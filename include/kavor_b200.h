@@ -163,14 +163,19 @@ int kvb_paged_decode_attn_no_alloc(const void* q, int64_t q_stride_t, int64_t q_
  * [0, cu_seqlens_k[b+1] - cu_seqlens_k[b]) with bottom-right causal alignment.
  * Keys come from the paged cache through block_tables (prefix cache / chunked
  * prefill) when block_tables != NULL, else from the contiguous k/v rows
- * [cu_seqlens_k[b] + j] (k_stride_t/h, v_stride_t/h). q/out [total_q, Hq, hd]. */
+ * [cu_seqlens_k[b] + j] (k_stride_t/h, v_stride_t/h). q/out [total_q, Hq, hd].
+ * total_q (rows of q) and total_k (rows of the contiguous k/v; unused when
+ * paged) bound the kernel's TMA maps: with them, page sizes that are a
+ * multiple of 128 and 16-byte output rows, QK^T and PV run on tcgen05 with
+ * TMEM accumulators; with total_q = 0 (or other page sizes) the warp-MMA
+ * kernel runs instead. */
 int kvb_prefill_attn(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
                      int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h,
                      int64_t num_blocks, int64_t block_stride, int block_size, const int32_t* block_tables,
                      int64_t block_table_stride, int max_blocks_per_seq, const int32_t* cu_seqlens_q,
                      const int32_t* cu_seqlens_k, int batch, int max_seqlen_q, void* out, int64_t out_stride_t,
                      int64_t out_stride_h, int num_q_heads, int num_kv_heads, int head_dim, float scale,
-                     void* stream);
+                     int64_t total_q, int64_t total_k, void* stream);
 
 /* --------------------------------------------------------------------- GEMM */
 
@@ -235,6 +240,11 @@ int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t mu
                     size_t max_bytes, void** comm);
 /* 1 when the communicator has a multicast mapping (switch-reduced modes). */
 int kvb_comm_has_multicast(void* comm);
+/* This rank's result rows of the switch two-shot mode: passing them (from row
+ * 0) as out / residual_out of kvb_allreduce_add_rmsnorm lets the kernel leave
+ * the reduced rows where the switch delivered them instead of copying them
+ * out; they stay valid until the next all-reduce call of the group. */
+int kvb_comm_result_rows(void* comm, void** out_rows, void** residual_rows);
 
 /* Fused all-reduce + residual add + RMSNorm over the TP group
  * (linear.py:156-160 followed by layernorm.py:114-140; with residual_in =

@@ -242,9 +242,11 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens_q: torch.Tensor,
                       cu_seqlens_k: torch.Tensor, max_seqlen_q: int, scale: float,
-                      block_tables: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                      block_tables: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                      tensor_cores: bool = True) -> torch.Tensor:
     """flash_attention_kvcache.py:73-79. With block_tables, k/v are the paged caches
-    [num_blocks, block_size, Hkv, hd]; otherwise contiguous-row [total_k, Hkv, hd] views."""
+    [num_blocks, block_size, Hkv, hd]; otherwise contiguous-row [total_k, Hkv, hd] views.
+    tensor_cores=False forces the warp-MMA kernel (the tcgen05 one is the default)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _cuda(t, n, _BF16)
     _cuda(cu_seqlens_q, "cu_seqlens_q", torch.int32)
@@ -262,14 +264,15 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
                   0, 0, nblk, k.stride(0), bs, block_tables.data_ptr(), block_tables.stride(0),
                   block_tables.shape[1], cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch,
                   int(max_seqlen_q), out.data_ptr(), out.stride(0), out.stride(1), Hq, Hkv, hd, float(scale),
-                  _stream())
+                  T if tensor_cores else 0, 0, _stream())
     else:
         Hkv = k.shape[1]
         _req(k.stride(-1) == 1 and v.stride(-1) == 1, "k/v last dim must be contiguous")
         _lib.call("kvb_prefill_attn", q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
                   k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), 0, 0, 0, None, 0, 0,
                   cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), batch, int(max_seqlen_q), out.data_ptr(),
-                  out.stride(0), out.stride(1), Hq, Hkv, hd, float(scale), _stream())
+                  out.stride(0), out.stride(1), Hq, Hkv, hd, float(scale), T if tensor_cores else 0,
+                  k.shape[0] if tensor_cores else 0, _stream())
     return out
 
 

@@ -34,7 +34,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_paged_decode_attn_workspace_size": [I, I, I, I, I, I, I, POINTER(c_size_t)],
     "kvb_paged_decode_attn": [P, L, L, P, P, L, L, I, P, L, I, P, P, L, L, I, I, I, I, F, I, P, c_size_t, P],
     "kvb_paged_decode_attn_no_alloc": [P, L, L, P, P, L, L, I, P, L, I, P, P, L, L, I, I, I, I, F, I, P],
-    "kvb_prefill_attn": [P, L, L, P, L, L, P, L, L, L, L, I, P, L, I, P, P, I, I, P, L, L, I, I, I, F, P],
+    "kvb_prefill_attn": [P, L, L, P, L, L, P, L, L, L, L, I, P, L, I, P, P, I, I, P, L, L, I, I, I, F, L, L, P],
     "kvb_sample": [P, L, P, P, P, I, I, P],
     "kvb_sample_partial": [P, L, P, P, P, P, I, I, L, L, P],
     "kvb_sample_combine": [P, P, I, P, I, P],
@@ -51,6 +51,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_comm_area_size": [c_size_t, POINTER(c_size_t)],
     "kvb_comm_attach": [I, I, POINTER(ctypes.c_uint64), ctypes.c_uint64, c_size_t, c_size_t, POINTER(c_void_p)],
     "kvb_comm_has_multicast": [P],
+    "kvb_comm_result_rows": [P, POINTER(c_void_p), POINTER(c_void_p)],
     "kvb_allreduce_add_rmsnorm": [P, I, P, P, P, P, I, I, F, I, P],
 }
 
@@ -58,7 +59,7 @@ _lib: ctypes.CDLL | None = None
 
 # Entry points that only query or report (everything else launches kernels).
 _QUERIES = {"kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
-            "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach", "kvb_comm_has_multicast", "kvb_comm_create", "kvb_comm_open_peers",
+            "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach", "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_comm_create", "kvb_comm_open_peers",
             "kvb_comm_data_buffer", "kvb_comm_destroy"}
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.

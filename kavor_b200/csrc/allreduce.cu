@@ -42,6 +42,7 @@ constexpr int kThreads = 256;
 constexpr int kMaxChunks = 8;  // hidden <= 256 threads x 8 chunks x 8 = 16384
 constexpr int kNumData = 3;
 constexpr size_t kFlagBytes = 2ull * kMaxBlocks * kMaxRanks * sizeof(uint32_t);
+constexpr size_t kMcFlagBytes = 2ull * kMaxBlocks * sizeof(uint32_t);  // switch-reduced arrival counters
 
 struct Comm {
   int rank = 0, world = 1, device = 0;
@@ -49,13 +50,14 @@ struct Comm {
   uint8_t* base = nullptr;  // local symmetric allocation
   uint8_t* peer[kMaxRanks] = {};
   uint8_t* mc = nullptr;    // NVLink multicast mapping of the area (NULL: none)
-  uint32_t* counters = nullptr;
+  uint32_t* counters = nullptr;     // [kMaxBlocks] calls per block (peer flag rounds)
+  uint32_t* mc_counters = nullptr;  // [kMaxBlocks] calls per block (switch flag rounds)
   bool opened[kMaxRanks] = {};
   bool owns_area = true;    // false: the area was attached (allocated and mapped by the caller)
 };
 
 struct Layout {
-  size_t flags, data[kNumData], result, total;
+  size_t flags, mc_flags, data[kNumData], result, total;
 };
 
 inline Layout layout_of(size_t data_bytes) {
@@ -63,6 +65,8 @@ inline Layout layout_of(size_t data_bytes) {
   size_t off = 0;
   L.flags = off;
   off += (kFlagBytes + 255) & ~size_t(255);
+  L.mc_flags = off;
+  off += (kMcFlagBytes + 255) & ~size_t(255);
   for (int i = 0; i < kNumData; ++i) {
     L.data[i] = off;
     off += (data_bytes + 255) & ~size_t(255);
@@ -78,6 +82,10 @@ struct ArArgs {
   bf16* result[kMaxRanks];        // every rank's result area (two-shot)
   uint32_t* flags[kMaxRanks];     // every rank's flag area
   uint32_t* counters;             // this rank's private counters
+  uint32_t* mc_counters;          // this rank's private counters of switch flag rounds
+  uint32_t* mc_flags;             // multicast address of the arrival counters (NVLS modes)
+  uint32_t* local_mc_flags;       // this rank's copy of them
+  int skip_out_copy, skip_res_copy;  // NVLS two-shot: out / residual_out are this rank's result rows
   const bf16* residual_in;        // NULL: first layer (residual := reduced sum)
   bf16* residual_out;
   bf16* out;
@@ -142,6 +150,33 @@ __device__ bool flag_round(const ArArgs& a, int phase, uint32_t v, bool publish,
     if (ld_acquire(f) != v) {
       const long long t0 = clock64();
       while (ld_acquire(f) != v) {
+        if (clock64() - t0 > kSpinCycles) {
+          atomicOr(&g_err_allreduce, (unsigned)kErrPeerTimeout);
+          *ok_s = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return *ok_s != 0;
+}
+
+// Switch flag round: thread 0 adds 1 to block b's arrival counter on every
+// rank at once (multimem.red through the NVSwitch) and waits until its own
+// copy reaches W x (calls of this block so far). `publish`: a system-scope
+// release fence first orders the block's multicast stores before the arrival.
+__device__ bool mc_round(const ArArgs& a, int phase, uint32_t target, bool publish, int* ok_s) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *ok_s = 1;
+    uint32_t* mc = a.mc_flags + (size_t)phase * kMaxBlocks + blockIdx.x;
+    if (publish) asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("multimem.red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(1u) : "memory");
+    const uint32_t* f = a.local_mc_flags + (size_t)phase * kMaxBlocks + blockIdx.x;
+    if ((int)(ld_acquire(f) - target) < 0) {
+      const long long t0 = clock64();
+      while ((int)(ld_acquire(f) - target) < 0) {
         if (clock64() - t0 > kSpinCycles) {
           atomicOr(&g_err_allreduce, (unsigned)kErrPeerTimeout);
           *ok_s = 0;
@@ -280,8 +315,8 @@ __device__ void copy_rows(const ArArgs& a, int t, const bf16* src) {
   for (int i = 0; i < NCH; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < nch) {
-      doo[c] = bo[i];
-      dr[c] = br[i];
+      if (!a.skip_out_copy) doo[c] = bo[i];
+      if (!a.skip_res_copy) dr[c] = br[i];
     }
   }
 }
@@ -294,30 +329,40 @@ __global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __gri
   __shared__ uint32_t v_s;
   __shared__ int ok_s;
   if (threadIdx.x == 0) {
-    v_s = a.counters[blockIdx.x] + 1;
-    a.counters[blockIdx.x] = v_s;
+    uint32_t* ctr = a.nvls ? a.mc_counters : a.counters;
+    v_s = ctr[blockIdx.x] + 1;
+    ctr[blockIdx.x] = v_s;
   }
   __syncthreads();
   const uint32_t v = v_s;
-  if (!flag_round<W>(a, 0, v, false, &ok_s)) return;
   const int nb = gridDim.x;
   const int64_t H = a.hidden;
-  if (a.nvls == 1) {  // every rank reduces every row through the switch
-    for (int t = blockIdx.x; t < a.tokens; t += nb)
-      reduce_row<W, NCH, true, false>(a, t, a.out + t * H, a.residual_out + t * H, red);
-    return;
-  }
-  if (a.nvls == 2) {  // rank r reduces rows t % W == r through the switch and multicasts them
-    for (int t = blockIdx.x; t < a.tokens; t += nb) {
-      if (t % W != a.rank) continue;
+  if (a.nvls) {
+    const uint32_t target = (uint32_t)W * v;  // v counts this block's switch rounds (mc_counters)
+    if (!mc_round(a, 0, target, false, &ok_s)) return;
+    if (a.nvls == 1) {  // every rank reduces every row through the switch
+      for (int t = blockIdx.x; t < a.tokens; t += nb)
+        reduce_row<W, NCH, true, false>(a, t, a.out + t * H, a.residual_out + t * H, red);
+      return;
+    }
+    // two-shot: block b of rank r reduces rows (b + k nb) W + r through the
+    // switch and multicasts out + residual rows into every rank's result area
+    for (int g = blockIdx.x; g * W < a.tokens; g += nb) {
+      const int t = g * W + a.rank;
+      if (t >= a.tokens) continue;
       bf16* o = a.mc_result + t * H;
       reduce_row<W, NCH, true, true>(a, t, o, o + a.result_stride, red);
     }
-    __syncthreads();
-    if (!flag_round<W>(a, 1, v, true, &ok_s)) return;
-    for (int t = blockIdx.x; t < a.tokens; t += nb) copy_rows<NCH>(a, t, a.result[a.rank] + t * H);
+    if (!mc_round(a, 1, target, true, &ok_s)) return;
+    if (a.skip_out_copy && a.skip_res_copy) return;  // the caller reads the result rows in place
+    for (int g = blockIdx.x; g * W < a.tokens; g += nb)
+      for (int p = 0; p < W; ++p) {
+        const int t = g * W + p;
+        if (t < a.tokens) copy_rows<NCH>(a, t, a.result[a.rank] + t * H);
+      }
     return;
   }
+  if (!flag_round<W>(a, 0, v, false, &ok_s)) return;
   if (!a.two_shot) {
     for (int t = blockIdx.x; t < a.tokens; t += nb)
       reduce_row<W, NCH, false, false>(a, t, a.out + t * H, a.residual_out + t * H, red);
@@ -370,8 +415,9 @@ extern "C" int kvb_comm_create(int rank, int world, size_t max_bytes, void** com
   const Layout L = layout_of(max_bytes);
   e = cudaMalloc(&c->base, L.total);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, kFlagBytes);
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, kMaxBlocks * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) c->mc_counters = c->counters + kMaxBlocks;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), c->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -451,8 +497,9 @@ extern "C" int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, 
   for (int p = 0; p < world; ++p) c->peer[p] = reinterpret_cast<uint8_t*>(peer_bases[p]);
   c->mc = reinterpret_cast<uint8_t*>(multicast_base);
   cudaError_t e = cudaGetDevice(&c->device);
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, kMaxBlocks * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) c->mc_counters = c->counters + kMaxBlocks;
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (c->counters) cudaFree(c->counters);
@@ -460,6 +507,15 @@ extern "C" int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, 
     return cuda_status(e, "kvb_comm_attach");
   }
   *comm = c;
+  return kOk;
+}
+
+extern "C" int kvb_comm_result_rows(void* comm, void** out_rows, void** residual_rows) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || !out_rows || !residual_rows) return set_error(kInvalid, "kvb_comm_result_rows: bad arguments");
+  const Layout L = layout_of(c->data_bytes);
+  *out_rows = c->base + L.result;
+  *residual_rows = c->base + L.result + ((c->data_bytes + 255) & ~size_t(255));
   return kOk;
 }
 
@@ -494,6 +550,9 @@ extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void*
     a.flags[p] = v ? reinterpret_cast<uint32_t*>(c->peer[p] + L.flags) : nullptr;
   }
   a.counters = c->counters;
+  a.mc_counters = c->mc_counters;
+  a.mc_flags = c->mc ? reinterpret_cast<uint32_t*>(c->mc + L.mc_flags) : nullptr;
+  a.local_mc_flags = reinterpret_cast<uint32_t*>(c->base + L.mc_flags);
   a.residual_in = (const bf16*)residual_in;
   a.residual_out = (bf16*)residual_out;
   a.out = (bf16*)out;
@@ -516,7 +575,14 @@ extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void*
   a.mc_result = c->mc ? reinterpret_cast<bf16*>(c->mc + L.result) : nullptr;
   a.result_stride = ((c->data_bytes + 255) & ~size_t(255)) / 2;
   a.eps = eps;
-  const int blocks = tokens < kMaxBlocks ? tokens : kMaxBlocks;
+  const size_t res_off = ((c->data_bytes + 255) & ~size_t(255));
+  a.skip_out_copy = out == c->base + L.result;
+  a.skip_res_copy = residual_out == c->base + L.result + res_off;
+  if (a.nvls != 2 && (a.skip_out_copy || a.skip_res_copy))
+    return set_error(kInvalid, "kvb_allreduce_add_rmsnorm: out / residual_out in the result area need the switch two-shot mode");
+  // rows per block: one row (one-shot, peer two-shot) or one group of W rows (switch two-shot)
+  const int rows = a.nvls == 2 ? (tokens + c->world - 1) / c->world : tokens;
+  const int blocks = rows < kMaxBlocks ? rows : kMaxBlocks;
   const int nch = hidden / 8;
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e;

@@ -77,6 +77,11 @@ class TPAllReduce:
             _lib.call("kvb_comm_data_buffer", self.comm, i, ctypes.byref(ptr), ctypes.byref(nbytes))
             raw = torch.as_tensor(_CudaArray(ptr.value, nbytes.value), device=device)
             self.buffers.append(raw.view(torch.bfloat16).view(max_tokens, hidden))
+        po, pr = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.call("kvb_comm_result_rows", self.comm, ctypes.byref(po), ctypes.byref(pr))
+        self.result_out, self.result_res = (
+            torch.as_tensor(_CudaArray(p.value, max_bytes), device=device).view(torch.bfloat16).view(max_tokens, hidden)
+            for p in (po, pr))
         dist.barrier(group=group)
         self._next = 0
 
@@ -98,8 +103,11 @@ class TPAllReduce:
         area = symm_mem.empty(int(n.value), dtype=torch.uint8, device=self.device)
         area.zero_()
         handle = symm_mem.rendezvous(area, group if group is not None else dist.group.WORLD)
-        ptrs = [int(p) for p in handle.buffer_ptrs]
+        # the tensor may sit at an offset inside the symmetric allocation
+        off = area.data_ptr() - int(handle.buffer_ptrs[self.rank])
+        ptrs = [int(p) + off for p in handle.buffer_ptrs]
         mc = int(handle.multicast_ptr) if getattr(handle, "multicast_ptr", 0) else 0
+        mc = mc + off if mc else 0
         arr = (ctypes.c_uint64 * self.world)(*ptrs)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
@@ -122,14 +130,28 @@ class TPAllReduce:
 
     def reduce_norm(self, index: int, tokens: int, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
                     mode: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
-        """(RMSNorm(sum + residual), sum + residual) with the residual updated in place."""
-        out = torch.empty(tokens, self.hidden, dtype=torch.bfloat16, device=self.device)
-        res_out = residual if residual is not None else torch.empty_like(out)
+        """(RMSNorm(sum + residual), sum + residual) with the residual updated in
+        place. In the switch two-shot mode both come back as views of this
+        rank's result rows (where the NVSwitch delivered them), valid until the
+        next call."""
+        mode = mode or self.mode
+        if self.switch_two_shot(tokens, mode):
+            out, res_out = self.result_out[:tokens], self.result_res[:tokens]
+            mode = 4
+        else:
+            out = torch.empty(tokens, self.hidden, dtype=torch.bfloat16, device=self.device)
+            res_out = residual if residual is not None else torch.empty_like(out)
+            if res_out.data_ptr() == self.result_res.data_ptr():  # the residual stream leaves the result rows
+                res_out = torch.empty_like(out)
         _lib.call("kvb_allreduce_add_rmsnorm", self.comm, index,
                   residual.data_ptr() if residual is not None else None, res_out.data_ptr(), out.data_ptr(),
-                  weight.data_ptr(), tokens, self.hidden, float(eps), mode or self.mode,
-                  torch.cuda.current_stream().cuda_stream)
+                  weight.data_ptr(), tokens, self.hidden, float(eps), mode, torch.cuda.current_stream().cuda_stream)
         return out, res_out
+
+    def switch_two_shot(self, tokens: int, mode: int = 0) -> bool:
+        """The library's automatic choice (and mode 4): reduce 1/W of the rows
+        in the switch and multicast them, from 8 rows per rank up."""
+        return self.multicast and (mode == 4 or (mode == 0 and self.world > 2 and tokens >= 8 * self.world))
 
     def close(self, group=None) -> None:
         """Collective: every rank's kernels that read this rank's buffers must

@@ -1,0 +1,101 @@
+"""GEMM sweep over the Qwen3-8B decode projections: kvb_gemm_bf16 (automatic
+plan and every forced K split), kvb_gemm_silu_bf16 for the gate-up shapes, and
+cuBLAS (torch.matmul) on the same operands.
+
+    python -m kavor_b200.profile_gemm [M,M,...]      (default 1,64,256)
+
+Shapes: QKV, O, gate-up, down and LM head of Qwen3-8B at TP=1 and TP=8. Each
+timing is one replay of a CUDA graph of 20 launches (device time, CUDA events),
+rotating over enough weight copies (>= 400 MB) that no launch finds its weight
+in L2. Prints one JSON line per (M, shape): [us, GB/s of weight + x + y bytes,
+token tile, max |y - cuBLAS|] per variant, then prefill-size lines (M = 2048,
+8192) in TFLOP/s.
+"""
+from __future__ import annotations
+
+import json
+import sys
+
+import torch
+
+from kavor_b200 import _kernels as K
+from kavor_b200 import _lib
+
+
+def _timeit(fn, iters=20):
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3
+
+
+def main(argv=None) -> int:
+    argv = sys.argv[1:] if argv is None else argv
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    shapes = []
+    for tp in (1, 8):
+        for name, N, Kd in (("qkv", 6144 // tp, 4096), ("o", 4096, 4096 // tp), ("gate_up", 24576 // tp, 4096),
+                            ("down", 4096, 12288 // tp), ("lm_head", 151936 // tp, 4096)):
+            shapes.append((f"{name}_tp{tp}", N, Kd))
+    Ms = [int(x) for x in argv[0].split(",")] if argv else [1, 64, 256]
+    for M in Ms:
+        for name, N, Kd in shapes:
+            wbytes = N * Kd * 2
+            copies = max(2, -(-400_000_000 // wbytes))
+            ws = [(torch.randn(N, Kd, device=dev) * 0.02).to(torch.bfloat16) for _ in range(min(copies, 16))]
+            x = torch.randn(M, Kd, device=dev).to(torch.bfloat16)
+            out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            ref = torch.matmul(x, ws[0].t())
+            res = {"M": M, "shape": name, "N": N, "K": Kd, "copies": len(ws), "plan": K.gemm_plan(M, N, Kd)}
+            nbytes = wbytes + M * Kd * 2 + M * N * 2
+            for label, splits in (("auto", 0), ("s1", 1), ("s2", 2), ("s4", 4), ("s8", 8), ("s16", 16)):
+                p = K.gemm_plan(M, N, Kd, splits)
+                if splits and p["splits"] != splits:
+                    continue
+                K.gemm(x, ws[0], out=out, splits=splits)
+                err = (out.float() - ref.float()).abs().max().item()
+                t = _timeit(lambda i: K.gemm(x, ws[i % len(ws)], out=out, splits=splits))
+                res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"], round(err, 4)]
+            t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
+            res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
+            if name.startswith("gate_up"):
+                og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+                for label, splits in (("g_auto", 0), ("g_s1", 1), ("g_s2", 2), ("g_s4", 4), ("g_s8", 8)):
+                    p = K.gemm_plan(M, N // 2, Kd, splits, True)
+                    if splits and p["splits"] != splits:
+                        continue
+                    t = _timeit(lambda i: K.gemm_silu(x, ws[i % len(ws)], out=og, splits=splits))
+                    res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"]]
+            res["device_error_bits"] = _lib.device_error(clear=True)
+            print(json.dumps(res), flush=True)
+            del ws
+            torch.cuda.empty_cache()
+    for M in (2048, 8192):
+        for name, N, Kd in (("qkv_tp1", 6144, 4096), ("gate_up_tp1", 24576, 4096), ("down_tp1", 4096, 12288)):
+            w = (torch.randn(N, Kd, device=dev) * 0.02).to(torch.bfloat16)
+            x = torch.randn(M, Kd, device=dev).to(torch.bfloat16)
+            out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            res = {"M": M, "shape": name, "N": N, "K": Kd, "plan": K.gemm_plan(M, N, Kd)}
+            res["auto_us"] = _timeit(lambda i: K.gemm(x, w, out=out), 10)
+            res["cublas_us"] = _timeit(lambda i: torch.matmul(x, w.t(), out=out), 10)
+            for k in ("auto", "cublas"):
+                res[k + "_tflops"] = 2 * M * N * Kd / res[k + "_us"] / 1e6
+            print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,7 +1,7 @@
 """Microbenchmark one kavor_b200 kernel on a synthetic case (used for ncu captures).
 
     python -m kavor_b200.profile_kernels decode_attn --batch 64 --context 1024 --hq 32 --hkv 8
-    python -m kavor_b200.profile_kernels prefill_attn --batch 4 --context 2048 --hq 32 --hkv 8
+    python -m kavor_b200.profile_kernels prefill_attn[_warp_mma] --batch 4 --context 2048 --hq 32 --hkv 8
     python -m kavor_b200.profile_kernels qknorm_rope_store|add_rmsnorm|silu_mul|sample --batch 256
     python -m kavor_b200.profile_kernels gemm --batch M --inter N --hidden K   (gemm_cublas: torch/cuBLAS)
 
@@ -40,7 +40,7 @@ def _decode_attn(a, dev):
     return run, nbytes, 0
 
 
-def _prefill_attn(a, dev):
+def _prefill_attn(a, dev, tensor_cores=True):
     hd = 128
     T = a.batch * a.context
     qkv = [torch.randn(T, (a.hq + 2 * a.hkv) * hd, device=dev).to(torch.bfloat16) for _ in range(a.copies)]
@@ -51,7 +51,8 @@ def _prefill_attn(a, dev):
     def run(i):
         x = qkv[i % len(qkv)]
         K.prefill_attention(x[:, :a.hq * hd].view(T, a.hq, hd), x[:, a.hq * hd:(a.hq + a.hkv) * hd].view(T, a.hkv, hd),
-                            x[:, (a.hq + a.hkv) * hd:].view(T, a.hkv, hd), cu, cu, a.context, hd ** -0.5, out=out)
+                            x[:, (a.hq + a.hkv) * hd:].view(T, a.hkv, hd), cu, cu, a.context, hd ** -0.5, out=out,
+                            tensor_cores=tensor_cores)
 
     return run, 2 * (qkv[0].numel() + out.numel()), flops
 
@@ -127,7 +128,9 @@ def _gemm(a, dev, use_torch=False):
     return run, 2 * (N * K_ + M * K_ + M * N), 2 * M * N * K_
 
 
-CASES = {"decode_attn": _decode_attn, "prefill_attn": _prefill_attn, "qknorm_rope_store": _qknorm_rope_store,
+CASES = {"decode_attn": _decode_attn, "prefill_attn": _prefill_attn,
+         "prefill_attn_warp_mma": lambda a, dev: _prefill_attn(a, dev, tensor_cores=False),
+         "qknorm_rope_store": _qknorm_rope_store,
          "add_rmsnorm": _add_rmsnorm, "silu_mul": _silu_mul, "sample": _sample, "gemm": _gemm,
          "gemm_cublas": lambda a, dev: _gemm(a, dev, use_torch=True)}
 

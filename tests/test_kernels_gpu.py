@@ -210,8 +210,9 @@ def test_decode_attention_is_invariant_to_split_count():
 
 
 # ------------------------------------------------------------------ prefill attention
-def test_varlen_prefill_contiguous_matches_oracle():
-    lens = [1, 77, 300, 64]
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_varlen_prefill_contiguous_matches_oracle(tensor_cores):
+    lens = [1, 77, 300, 64, 129]
     hq, hkv = 16, 8
     T = sum(lens)
     qkv = torch.randn(T, (hq + 2 * hkv) * 128, generator=g(40)).to(torch.bfloat16)
@@ -223,16 +224,18 @@ def test_varlen_prefill_contiguous_matches_oracle():
     d = qkv.to(DEV)
     out = K().prefill_attention(d[:, :hq * 128].view(T, hq, 128), d[:, hq * 128:(hq + hkv) * 128].view(T, hkv, 128),
                                 d[:, (hq + hkv) * 128:].view(T, hkv, 128), cu.to(DEV), cu.to(DEV), max(lens),
-                                128 ** -0.5)
+                                128 ** -0.5, tensor_cores=tensor_cores)
     close(out, ref)
 
 
-def test_paged_prefill_with_cached_prefix_matches_oracle():
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_paged_prefill_with_cached_prefix_matches_oracle(tensor_cores):
     """Chunked prefill / prefix-cache hit: new queries attend cached keys too
-    (bottom-right causal alignment)."""
+    (bottom-right causal alignment). Cache bytes past each sequence are NaN:
+    neither kernel may let them reach the output."""
     hq, hkv, bs = 32, 8, 256
-    cached = [256, 0, 512, 100]
-    new = [100, 50, 300, 1]
+    cached = [256, 0, 512, 100, 0]
+    new = [100, 50, 300, 1, 700]
     kv_len = [c + n for c, n in zip(cached, new)]
     need = [(x + bs - 1) // bs for x in kv_len]
     nblk = sum(need) + 1
@@ -243,6 +246,9 @@ def test_paged_prefill_with_cached_prefix_matches_oracle():
         tables.append(perm[j:j + n] + [-1] * (width - n))
         j += n
     pool = torch.randn(nblk, 2, bs, hkv, 128, generator=g(42)).to(torch.bfloat16)
+    for row, n in zip(tables, kv_len):  # stale bytes after the last key of each sequence
+        last = row[(n - 1) // bs]
+        pool[last, :, (n - 1) % bs + 1:] = float("nan")
     T = sum(new)
     q = torch.randn(T, hq, 128, generator=g(43)).to(torch.bfloat16)
     cu_q = torch.tensor([0] + torch.tensor(new).cumsum(0).tolist(), dtype=torch.int32)
@@ -251,7 +257,8 @@ def test_paged_prefill_with_cached_prefix_matches_oracle():
     ref = ops.varlen_prefill_attention(q, pool[:, 0], pool[:, 1], cu_q, cu_k, 128 ** -0.5, bt)
     dpool = pool.to(DEV)
     out = K().prefill_attention(q.to(DEV), dpool[:, 0], dpool[:, 1], cu_q.to(DEV), cu_k.to(DEV), max(new),
-                                128 ** -0.5, block_tables=bt.to(DEV))
+                                128 ** -0.5, block_tables=bt.to(DEV), tensor_cores=tensor_cores)
+    assert not out.isnan().any()
     close(out, ref)
 
 

@@ -246,6 +246,18 @@ def step_bytes(shape: dict, tp: int, batch: int, context: int) -> int:
     return weights + kv + 2 * batch * H
 
 
+def allreduce_bus_bytes(shape: dict, tp: int, batch: int) -> float:
+    """Bytes each rank must move over NVLink per decode step: 2L+1 all-reduces
+    of [batch, hidden] bf16, each 2 (N-1)/N of the tensor (ring / two-shot)."""
+    if tp <= 1:
+        return 0.0
+    L, H = shape["num_hidden_layers"], shape["hidden_size"]
+    return (2 * L + 1) * 2 * (tp - 1) / tp * batch * H * 2
+
+
+NVLINK_GBS = 900.0  # nominal per direction per GPU (the roofline's all-reduce term)
+
+
 def attention_bytes(batch: int, context: int, hq: int, hkv: int) -> int:
     """Algorithmic bytes of one decode-attention launch: K and V of every
     context token once, q read and o written."""
@@ -376,8 +388,12 @@ def run_ours(args) -> int:
                 "algorithmic_bytes": a_bytes, "avg_launch_us": t_attn * 1e6}
     s_bytes = step_bytes(shape, world, B, ctx0)
     t_roof = s_bytes / (peak * 1e9)
-    step_roof = {"bytes_per_rank": s_bytes, "t_hbm_us": t_roof * 1e6, "frac": t_roof / (ms_per_step / 1e3),
-                 "peak_gbs": peak, "peak_source": peak_src}
+    ar_bytes = allreduce_bus_bytes(shape, world, B)
+    t_ar = ar_bytes / (NVLINK_GBS * 1e9)
+    t_step_roof = max(t_roof, t_ar)  # the slower of weight+KV bytes at HBM peak and all-reduce bytes over NVLink
+    step_roof = {"bytes_per_rank": s_bytes, "t_hbm_us": t_roof * 1e6, "allreduce_bytes_per_rank": ar_bytes,
+                 "t_nvlink_us": t_ar * 1e6, "nvlink_gbs": NVLINK_GBS, "t_roofline_us": t_step_roof * 1e6,
+                 "frac": t_step_roof / (ms_per_step / 1e3), "peak_gbs": peak, "peak_source": peak_src}
 
     # --- end to end through ModelRunner.run (sequences advance one token per step)
     e2e = None

@@ -316,11 +316,15 @@ int encode_kv_map(CUtensorMap* map, const void* base, int64_t num_blocks, int64_
   return kOk;
 }
 
+// Split the context only when (sequence, kv head) units leave more than half
+// of the 2-per-SM CTA slots idle, and then into as many parts as one wave
+// holds: at B=256 x 1 kv head (TP=8) one unsplit wave measured 23 us against
+// 40 us split three ways (the extra wave, the partial traffic and the merge).
 int choose_splits(int batch, int hkv, int max_tiles, int sms) {
   const int units = batch * hkv;
   const int slots = 2 * sms;  // two CTAs fit per SM
-  if (units >= slots || max_tiles <= 1) return 1;
-  int s = (2 * slots + units - 1) / units;
+  if (2 * units >= slots || max_tiles <= 1) return 1;
+  int s = slots / units;
   if (s > max_tiles) s = max_tiles;
   if (s > 64) s = 64;
   return s < 1 ? 1 : s;

@@ -73,15 +73,24 @@ def _worker(rank, world, port, results, backend):
                     res = _partial(7, T, salt) if with_res else None
                     ar.partial_buffer(idx, T).copy_(_partial(rank, T, salt).to(dev))
                     dres = res.to(dev) if res is not None else None
+                    # ranks reach the call together: the kernel's peer wait is bounded
+                    # (~1 s) and the oracle work between calls is host time
+                    torch.cuda.synchronize()
+                    dist.barrier()
                     out, r = ar.reduce_norm(idx, T, dres, dw, 1e-6, mode=mode)
                     idx ^= 1
+                    bits = _lib.device_error(clear=True)
+                    if bits:
+                        errors.append(f"device error bits {bits} after mode={mode} T={T} res={with_res}")
                     eo, er = _expected(T, salt, res, w, world)
                     # peer modes sum in fp32 in rank order and round once: bit-exact; the
-                    # switch (modes 3, 4) rounds its sum its own way: the reduced value may
-                    # differ by one bf16 ulp (2^-5 at |y| < 8), which the residual add keeps
-                    if mode <= 2 and not torch.equal(r.cpu(), er):
+                    # switch (modes 3, 4, and the automatic mode from 4 ranks up) reduces in
+                    # its own order and rounding: the reduced value may differ by a bf16 ulp
+                    # or two (2^-4 at |y| < 16), which the residual add keeps
+                    switch = mode > 2 or (mode == 0 and ar.multicast and world > 2)
+                    if not switch and not torch.equal(r.cpu(), er):
                         errors.append(f"residual mode={mode} T={T} res={with_res}")
-                    if mode > 2 and not torch.allclose(r.float().cpu(), er.float(), atol=3.2e-2, rtol=1e-2):
+                    if switch and not torch.allclose(r.float().cpu(), er.float(), atol=3.2e-2, rtol=2e-2):
                         errors.append(f"residual mode={mode} T={T} res={with_res} "
                                       f"max diff {(r.float().cpu() - er.float()).abs().max().item():.4f}")
                     if not torch.allclose(out.float().cpu(), eo.float(), atol=2e-2, rtol=2e-2):
@@ -100,6 +109,8 @@ def _worker(rank, world, port, results, backend):
             salt += 1
             resid.zero_()
             bufs[2].copy_(_partial(rank, T, salt).to(dev))
+            torch.cuda.synchronize()
+            dist.barrier()
             g.replay()
             torch.cuda.synchronize()
             e1, er1 = _expected(T, salt, torch.zeros(T, H, dtype=torch.bfloat16), w, world)
@@ -112,8 +123,9 @@ def _worker(rank, world, port, results, backend):
                 errors.append(f"graph replay {rep}: residual")
             if not torch.allclose(o2.float().cpu(), e2.float(), atol=2e-2, rtol=2e-2):
                 errors.append(f"graph replay {rep}: out")
-        if _lib.device_error(clear=True) != 0:
-            errors.append("device error bits after the parity runs")
+        bits = _lib.device_error(clear=True)
+        if bits:
+            errors.append(f"device error bits {bits} after the graph replays")
         # bounded wait (IPC area, peer one-shot only): rank 1 skips one call,
         # rank 0's kernel must give up and report it
         dist.barrier()

@@ -73,6 +73,10 @@ def _worker(rank, world, port, results):
             cu = torch.tensor([0] + torch.tensor([len(s) for s in seqs]).cumsum(0).tolist(), **i32)
             slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))], **i32)
             for step in range(5):
+                # ranks start each forward together (the fused all-reduce's peer wait
+                # is bounded at about a second; host work between steps is not)
+                torch.cuda.synchronize()
+                dist.barrier()
                 if step == 0:
                     set_context(True, cu, cu, max(map(len, seqs)), max(map(len, seqs)), slots)
                 else:

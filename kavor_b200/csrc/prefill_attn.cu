@@ -270,9 +270,9 @@ constexpr int kTcRows = 128;                    // query rows per CTA (UMMA M)
 constexpr int kTcKeys = 128;                    // keys per tile (UMMA N of QK^T, K of PV)
 constexpr int kTcHalf = 128 * 64 * 2;           // [128 rows][64 bf16] 128-byte-swizzled half tile
 constexpr int kTcTile = 2 * kTcHalf;            // 32 KB: 128 rows x 128 bf16
-constexpr int kTcQ = 0, kTcK = kTcTile, kTcV = 3 * kTcTile, kTcP = 5 * kTcTile;  // K, V: 2 stages each
-constexpr int kTcSmem = 6 * kTcTile + 1024;
-constexpr uint32_t kTcCols = 512;               // TMEM: S0 [0,128), S1 [128,256), PV [256,384)
+constexpr int kTcQ = 0, kTcK = kTcTile, kTcV = 3 * kTcTile, kTcP = 5 * kTcTile;  // K, V, P: 2 buffers each
+constexpr int kTcSmem = 7 * kTcTile + 1024;     // 225 KB
+constexpr uint32_t kTcCols = 512;               // TMEM: S0, S1, PV0, PV1 (128 columns each)
 
 struct TcArgs {
   int block_size;
@@ -349,8 +349,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, kfull[2], vfull[2], kv_empty[2], s_full[2], s_empty[2], p_full, pv_full,
-      pv_empty;
+  __shared__ __align__(8) uint64_t q_full, kfull[2], vfull[2], kv_empty[2], s_full[2], s_empty[2], p_full[2],
+      pv_full[2], pv_empty[2];
   __shared__ uint32_t tmem_s;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -377,10 +377,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(smem_u32(&kv_empty[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
       mbar_init(smem_u32(&s_empty[i]), 4);
+      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&pv_full[i]), 1);
+      mbar_init(smem_u32(&pv_empty[i]), 4);
     }
-    mbar_init(smem_u32(&p_full), 4);
-    mbar_init(smem_u32(&pv_full), 1);
-    mbar_init(smem_u32(&pv_empty), 4);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -463,18 +463,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (ok) ok = issue_s(0);
       for (int j = 0; j < ntiles && ok; ++j) {
         if (j + 1 < ntiles && !issue_s(j + 1)) break;
-        const int st = j & 1;
-        if (!mbar_wait(smem_u32(&p_full), j & 1, &g_err_prefill)) break;
+        const int st = j & 1, pb = j & 1;  // K/V stage, P and PV buffers of tile j
+        if (!mbar_wait(smem_u32(&p_full[pb]), (j >> 1) & 1, &g_err_prefill)) break;
         if (!mbar_wait(smem_u32(&vfull[st]), (j >> 1) & 1, &g_err_prefill)) break;
-        if (j >= 1 && !mbar_wait(smem_u32(&pv_empty), (j - 1) & 1, &g_err_prefill)) break;
+        if (j >= 2 && !mbar_wait(smem_u32(&pv_empty[pb]), ((j >> 1) - 1) & 1, &g_err_prefill)) break;
         tc_after();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // K = keys: 16 per step
-          const uint32_t pa = sbase + kTcP + (ks >> 2) * kTcHalf + (ks & 3) * 32;
+          const uint32_t pa = sbase + kTcP + pb * kTcTile + (ks >> 2) * kTcHalf + (ks & 3) * 32;
           const uint32_t vb = sbase + kTcV + st * kTcTile + ks * 2048;
-          tc_mma(tmem + 2 * kTcKeys, desc_kmajor(pa), desc_mnmajor(vb), a.idesc_pv, ks > 0);
+          tc_mma(tmem + (2 + pb) * kTcKeys, desc_kmajor(pa), desc_mnmajor(vb), a.idesc_pv, ks > 0);
         }
-        tc_commit(smem_u32(&pv_full));
+        tc_commit(smem_u32(&pv_full[pb]));
         tc_commit(smem_u32(&kv_empty[st]));
       }
     }
@@ -489,9 +489,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
     for (int i = 0; i < kHD; ++i) o[i] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
+    float corr_prev = 1.f;  // rescale of the tile whose P V is folded next
     bool ok = true;
+    // fold P V of tile t (computed relative to that tile's max) into O
+    auto fold = [&](int t, float corr) -> bool {
+      const int pb = t & 1;
+      if (!mbar_wait(smem_u32(&pv_full[pb]), (t >> 1) & 1, &g_err_prefill)) return false;
+      tc_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_base + (2 + pb) * kTcKeys + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * corr + v[i];
+      }
+      tc_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&pv_empty[pb]));
+      return true;
+    };
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int sb = j & 1, st = j & 1;
+      const int sb = j & 1, st = j & 1, pb = j & 1;
       const int key0 = j * kTcKeys;
       if (!mbar_wait(smem_u32(&s_full[sb]), (j >> 1) & 1, &g_err_prefill)) { ok = false; break; }
       tc_after();
@@ -512,6 +530,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float base = m_new == -INFINITY ? 0.f : m_new;
       const float corr = exp2f(m_run - base);
       float psum = 0.f;
+      // P buffer pb was last read by P V of tile j - 2, folded (waited for)
+      // in the previous iteration
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32];
@@ -527,7 +547,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           pk[i / 2] = pack_bf16(p0, p1);
         }
         // keys c*32 .. c*32+31 of row r: half c/2, 16-byte chunks (c%2)*4 .. +3
-        const uint32_t prow = sbase + kTcP + (c >> 1) * kTcHalf + r * 128;
+        const uint32_t prow = sbase + kTcP + pb * kTcTile + (c >> 1) * kTcHalf + r * 128;
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
           const int ch = (c & 1) * 4 + k4;
@@ -556,22 +576,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&p_full));
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
       l_run = l_run * corr + psum;
       m_run = m_new;
-      if (!mbar_wait(smem_u32(&pv_full), j & 1, &g_err_prefill)) { ok = false; break; }
-      tc_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_base + 2 * kTcKeys + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * corr + v[i];
-      }
-      tc_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&pv_empty));
+      // P V of this tile now runs on the tensor core; fold the previous one
+      if (j >= 1 && !fold(j - 1, corr_prev)) { ok = false; break; }
+      corr_prev = corr;
     }
+    if (ok && ntiles > 0 && !fold(ntiles - 1, corr_prev)) ok = false;
     if (qi < seqlen_q) {
       const float inv = (ok && l_run > 0.f) ? 1.f / l_run : 0.f;
       bf16* orow = a.out + (int64_t)(q_seq0 + qi) * a.o_st + (int64_t)h * a.o_sh;

@@ -296,6 +296,7 @@ class ModelRunner:
 
     @torch.inference_mode()
     def _profile_prefill(self) -> None:
+        self._sync_ranks()
         seq_len = min(self.config.max_num_batched_tokens, self.config.max_model_len)
         num_seqs = max(1, min(self.config.max_num_batched_tokens // seq_len, self.config.max_num_seqs))
         total = seq_len * num_seqs
@@ -312,6 +313,7 @@ class ModelRunner:
 
     @torch.inference_mode()
     def _profile_decode(self, bs: int) -> None:
+        self._sync_ranks()
         set_context(False, slot_mapping=torch.zeros(bs, dtype=torch.int32, device=self.device),
                     context_lens=torch.ones(bs, dtype=torch.int32, device=self.device),
                     block_tables=torch.zeros(bs, self.max_blocks_per_seq, dtype=torch.int32, device=self.device))
@@ -362,6 +364,13 @@ class ModelRunner:
                                   out=self.decode_buffers.sampled[:bs])
 
     @torch.inference_mode()
+    def _sync_ranks(self) -> None:
+        """Before a forward that runs the fused all-reduce during set-up: the
+        ranks' host work so far differs, and the kernel's peer wait is bounded."""
+        if self.world_size > 1:
+            torch.cuda.synchronize(self.device)
+            dist.barrier()
+
     def capture_cudagraph(self) -> None:
         max_bs = self._max_graph_bs()
         self.decode_buffers = DecodeBuffers(max_bs, self.max_blocks_per_seq, self.device)
@@ -379,6 +388,7 @@ class ModelRunner:
         for bs in reversed(self.graph_bs):
             set_context(False, slot_mapping=d["slot_mapping"][:bs], context_lens=d["context_lens"][:bs],
                         block_tables=d["block_tables"][:bs])
+            self._sync_ranks()
             self._decode_forward(bs)  # warm-up outside the graph
             graph = torch.cuda.CUDAGraph()
             calls0 = _lib.launch_count()
@@ -396,8 +406,26 @@ class ModelRunner:
         if not hasattr(self, "decode_buffers"):
             self.decode_buffers = DecodeBuffers(self._max_graph_bs(), self.max_blocks_per_seq, self.device)
 
+    # Every DEVICE_CHECK_EVERY steps the device-side error bits are read back
+    # (a synchronising query): a bounded wait that gave up (a peer that did not
+    # arrive within about a second), an index outside its buffer, ... raise
+    # here instead of going unnoticed.
+    DEVICE_CHECK_EVERY = 64
+
+    def _check_device(self) -> None:
+        self._steps = getattr(self, "_steps", 0) + 1
+        if self._steps % self.DEVICE_CHECK_EVERY:
+            return
+        bits = _lib.device_error(clear=True)
+        if bits:
+            names = {1: "block table", 2: "slot mapping", 4: "wait timeout", 8: "token id", 16: "peer wait timeout"}
+            what = ", ".join(n for b, n in names.items() if bits & b)
+            raise RuntimeError(f"rank {self.rank}: device-side error bits {bits:#x} ({what}) within the last "
+                               f"{self.DEVICE_CHECK_EVERY} steps")
+
     @torch.inference_mode()
     def run(self, seqs: list[Sequence], is_prefill: bool) -> list[int]:
+        self._check_device()
         temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
         if is_prefill:
             meta = prefill_metadata(seqs, self.block_size)

@@ -17,6 +17,7 @@ the decode graph at every TP size.
 from __future__ import annotations
 
 import datetime
+import itertools
 import os
 import pickle
 from multiprocessing.shared_memory import SharedMemory
@@ -39,24 +40,31 @@ SHM_BYTES = 1 << 22
 
 # ----------------------------------------------------------------- host metadata
 def block_table_matrix(seqs: list[Sequence], width: int | None = None) -> np.ndarray:
-    """[B, max blocks] int32, rows padded with -1 (model_runner.py:469-473)."""
-    w = max(len(s.block_table) for s in seqs) if width is None else width
+    """[B, max blocks] int32, rows padded with -1 (model_runner.py:469-473).
+    One flat gather of every table and one masked scatter (no per-row numpy
+    call: this runs on the host every decode step)."""
+    lens = np.fromiter((len(s.block_table) for s in seqs), np.int64, len(seqs))
+    w = int(lens.max(initial=0)) if width is None else width
     out = np.full((len(seqs), w), -1, dtype=np.int32)
-    for i, s in enumerate(seqs):
-        out[i, :len(s.block_table)] = s.block_table
+    flat = np.fromiter(itertools.chain.from_iterable(s.block_table for s in seqs), np.int32, int(lens.sum()))
+    out[np.arange(w) < lens[:, None]] = flat
     return out
 
 
 def decode_metadata(seqs: list[Sequence], block_size: int) -> dict[str, np.ndarray]:
     """model_runner.py:448-467: the last token of every sequence at position len-1,
-    written to slot block_table[-1]*block_size + last_block_num_tokens - 1."""
+    written to slot block_table[-1]*block_size + last_block_num_tokens - 1.
+    One pass over the sequences (token, length, last block id, tokens in it)."""
     n = len(seqs)
+    rows = np.fromiter(itertools.chain.from_iterable(
+        (s.last_token, s.num_tokens, s.block_table[-1]) for s in seqs), np.int64, 3 * n).reshape(n, 3)
+    ctx = rows[:, 1]
     return {
-        "input_ids": np.fromiter((s.last_token for s in seqs), np.int64, n),
-        "positions": np.fromiter((len(s) - 1 for s in seqs), np.int64, n),
-        "slot_mapping": np.fromiter(
-            (s.block_table[-1] * block_size + s.last_block_num_tokens - 1 for s in seqs), np.int32, n),
-        "context_lens": np.fromiter((len(s) for s in seqs), np.int32, n),
+        "input_ids": rows[:, 0].copy(),
+        "positions": ctx - 1,
+        # last_block_num_tokens - 1 == (len - 1) % block_size
+        "slot_mapping": (rows[:, 2] * block_size + (ctx - 1) % block_size).astype(np.int32),
+        "context_lens": ctx.astype(np.int32),
         "block_tables": block_table_matrix(seqs),
     }
 

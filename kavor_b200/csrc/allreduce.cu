@@ -51,7 +51,7 @@ struct Comm {
   uint8_t* peer[kMaxRanks] = {};
   uint8_t* mc = nullptr;    // NVLink multicast mapping of the area (NULL: none)
   uint32_t* counters = nullptr;     // [kMaxBlocks] calls per block (peer flag rounds)
-  uint32_t* mc_counters = nullptr;  // [kMaxBlocks] calls per block (switch flag rounds)
+  uint32_t* mc_counters = nullptr;  // [2][kMaxBlocks] calls per block that ran switch round 0 / round 1
   bool opened[kMaxRanks] = {};
   bool owns_area = true;    // false: the area was attached (allocated and mapped by the caller)
 };
@@ -82,7 +82,7 @@ struct ArArgs {
   bf16* result[kMaxRanks];        // every rank's result area (two-shot)
   uint32_t* flags[kMaxRanks];     // every rank's flag area
   uint32_t* counters;             // this rank's private counters
-  uint32_t* mc_counters;          // this rank's private counters of switch flag rounds
+  uint32_t* mc_counters;          // this rank's private counters: [phase][block] switch rounds run
   uint32_t* mc_flags;             // multicast address of the arrival counters (NVLS modes)
   uint32_t* local_mc_flags;       // this rank's copy of them
   int skip_out_copy, skip_res_copy;  // NVLS two-shot: out / residual_out are this rank's result rows
@@ -328,17 +328,24 @@ __global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __gri
   __shared__ float red[kThreads / 32];
   __shared__ uint32_t v_s;
   __shared__ int ok_s;
+  __shared__ uint32_t v1_s;
   if (threadIdx.x == 0) {
+    // each flag word counts its own rounds: the switch round-1 word only
+    // advances in two-shot calls, so it gets a counter of its own
     uint32_t* ctr = a.nvls ? a.mc_counters : a.counters;
     v_s = ctr[blockIdx.x] + 1;
     ctr[blockIdx.x] = v_s;
+    if (a.nvls == 2) {
+      v1_s = a.mc_counters[kMaxBlocks + blockIdx.x] + 1;
+      a.mc_counters[kMaxBlocks + blockIdx.x] = v1_s;
+    }
   }
   __syncthreads();
   const uint32_t v = v_s;
   const int nb = gridDim.x;
   const int64_t H = a.hidden;
   if (a.nvls) {
-    const uint32_t target = (uint32_t)W * v;  // v counts this block's switch rounds (mc_counters)
+    const uint32_t target = (uint32_t)W * v;  // round-0 word: W per switch call of this block
     if (!mc_round(a, 0, target, false, &ok_s)) return;
     if (a.nvls == 1) {  // every rank reduces every row through the switch
       for (int t = blockIdx.x; t < a.tokens; t += nb)
@@ -353,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __gri
       bf16* o = a.mc_result + t * H;
       reduce_row<W, NCH, true, true>(a, t, o, o + a.result_stride, red);
     }
-    if (!mc_round(a, 1, target, true, &ok_s)) return;
+    if (!mc_round(a, 1, (uint32_t)W * v1_s, true, &ok_s)) return;  // round-1 word: W per two-shot call
     if (a.skip_out_copy && a.skip_res_copy) return;  // the caller reads the result rows in place
     for (int g = blockIdx.x; g * W < a.tokens; g += nb)
       for (int p = 0; p < W; ++p) {
@@ -415,8 +422,8 @@ extern "C" int kvb_comm_create(int rank, int world, size_t max_bytes, void** com
   const Layout L = layout_of(max_bytes);
   e = cudaMalloc(&c->base, L.total);
   if (e == cudaSuccess) e = cudaMemset(c->base, 0, kFlagBytes);
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * kMaxBlocks * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 3 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 3 * kMaxBlocks * sizeof(uint32_t));
   if (e == cudaSuccess) c->mc_counters = c->counters + kMaxBlocks;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), c->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -497,8 +504,8 @@ extern "C" int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, 
   for (int p = 0; p < world; ++p) c->peer[p] = reinterpret_cast<uint8_t*>(peer_bases[p]);
   c->mc = reinterpret_cast<uint8_t*>(multicast_base);
   cudaError_t e = cudaGetDevice(&c->device);
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 2 * kMaxBlocks * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 2 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, 3 * kMaxBlocks * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, 3 * kMaxBlocks * sizeof(uint32_t));
   if (e == cudaSuccess) c->mc_counters = c->counters + kMaxBlocks;
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {

@@ -317,20 +317,6 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(kTcHalf >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// 2^x on the FMA pipe, for half of the softmax exponentials (the other half
-// stay on the MUFU unit, whose 16 results per clock per SM bound the softmax):
-// exponent split 2^x = 2^i 2^f with i = floor(x), f in [0, 1) (Cody-Waite
-// range reduction), and 2^f from a cubic fitted here by iteratively
-// reweighted least squares to minimise the relative error on [0, 1]: max
-// 8.6e-5, far below the 2^-8 resolution of the bf16 P it feeds.
-__device__ __forceinline__ float exp2_fma(float x) {
-  if (x < -126.f) return 0.f;
-  const float i = floorf(x);
-  const float f = x - i;
-  const float p = fmaf(fmaf(fmaf(0.07706705f, f, 0.227645f), f, 0.69511676f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + ((int)i << 23));
-}
-
 __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -556,7 +542,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int key = key0 + c * 32 + i;
           const float x0 = (key < kv_len && key <= lim) ? v[i] * a.scale_log2 : -INFINITY;
           const float x1 = (key + 1 < kv_len && key + 1 <= lim) ? v[i + 1] * a.scale_log2 : -INFINITY;
-          const float p0 = exp2f(x0 - base), p1 = exp2_fma(x1 - base);
+          const float p0 = exp2f(x0 - base), p1 = exp2f(x1 - base);
           psum += p0 + p1;
           pk[i / 2] = pack_bf16(p0, p1);
         }

@@ -1,0 +1,239 @@
+"""Host-side behaviour of Sequence, BlockManager and Scheduler, case by case —
+the behaviours the reference's own suite checks for the full-attention path
+(tests/test_sequence.py, test_block_manager.py, test_scheduler.py there), on
+this package's classes, with 4-token blocks. (The golden host trace in
+test_host_metadata.py checks the same classes end to end, bit-exact against a
+trace produced by the reference.)"""
+import pickle
+
+import pytest
+
+from kavor_b200.engine.block_manager import BlockManager
+from kavor_b200.engine.scheduler import Scheduler
+from kavor_b200.engine.sequence import SequenceStatus
+
+BS = 4
+
+
+# ------------------------------------------------------------------ Sequence
+def test_sequence_block_arithmetic(make_seq):
+    s = make_seq(range(1, 10))  # 9 tokens: blocks of 4, 4, 1
+    assert s.num_blocks == 3 and s.last_block_num_tokens == 1
+    assert s.block(0) == [1, 2, 3, 4] and s.block(2) == [9]
+    with pytest.raises(IndexError):
+        s.block(3)
+    full = make_seq(range(8))
+    assert full.num_blocks == 2 and full.last_block_num_tokens == 4
+
+
+def test_append_token_advances_counters(make_seq):
+    s = make_seq([5, 6, 7])
+    s.append_token(42)
+    assert len(s) == 4 and s.last_token == 42 and s.num_completion_tokens == 1
+    assert s.completion_token_ids == [42] and s.prompt_token_ids == [5, 6, 7]
+
+
+def test_pickle_sends_all_tokens_in_prefill_and_only_the_last_in_decode(make_seq):
+    s = make_seq(range(10, 20))
+    s.block_table = [3, 7, 1]
+    p = pickle.loads(pickle.dumps(s))
+    assert p.token_ids == list(range(10, 20)) and p.block_table == [3, 7, 1] and len(p) == 10
+    s.is_prefill = False
+    s.append_token(99)
+    d = pickle.loads(pickle.dumps(s))
+    assert d.token_ids == [] and d.last_token == 99 and len(d) == 11 and d.block_table == [3, 7, 1]
+
+
+# ------------------------------------------------------------------ BlockManager
+def _finish_prefill(bm, seq):
+    """Allocate, run the whole prompt as one step and key its full blocks."""
+    cached, _ = bm.can_allocate_prefill(seq)
+    bm.allocate_prefill(seq, cached)
+    seq.num_scheduled_tokens = len(seq) - seq.num_cached_tokens
+    bm.hash_blocks(seq)
+    seq.num_cached_tokens += seq.num_scheduled_tokens
+    seq.num_scheduled_tokens = 0
+    return cached
+
+
+def test_allocate_then_free_restores_the_pool(make_seq):
+    bm = BlockManager(8, BS)
+    s = make_seq(range(10))
+    bm.allocate_prefill(s, 0)
+    assert s.block_table == [0, 1, 2] and len(bm.free_block_ids) == 5
+    bm.deallocate(s)
+    assert s.block_table == [] and len(bm.free_block_ids) == 8 and not bm.used_block_ids
+    assert list(bm.free_block_ids)[-3:] == [2, 1, 0]  # freed last block first
+
+
+def test_prefix_of_a_finished_sequence_is_reused(make_seq):
+    bm = BlockManager(16, BS)
+    a = make_seq(list(range(12)) + [100])  # 3 full blocks + 1 token
+    _finish_prefill(bm, a)
+    table_a = list(a.block_table)
+    bm.deallocate(a)
+    b = make_seq(list(range(12)) + [200, 201])
+    cached, _ = bm.can_allocate_prefill(b)
+    bm.allocate_prefill(b, cached)
+    assert cached == 3 and b.block_table[:3] == table_a[:3] and b.num_cached_tokens == 12
+
+
+def test_prefix_hits_stop_at_the_first_divergent_block(make_seq):
+    bm = BlockManager(16, BS)
+    _finish_prefill(bm, make_seq(list(range(12)) + [1]))
+    b = make_seq([0, 1, 2, 3, 4, 5, 99, 7, 8, 9, 10, 11, 1])
+    assert bm.can_allocate_prefill(b)[0] == 1
+
+
+def test_the_last_block_of_a_prompt_is_never_served_from_the_cache(make_seq):
+    bm = BlockManager(16, BS)
+    _finish_prefill(bm, make_seq(range(8)))  # exactly two full blocks, both keyed
+    same = make_seq(range(8))
+    assert bm.can_allocate_prefill(same)[0] == 1  # its own last block is recomputed
+    longer = make_seq(list(range(8)) + [50])
+    assert bm.can_allocate_prefill(longer)[0] == 2  # but a longer prompt reuses both
+
+
+def test_a_key_whose_block_holds_other_tokens_is_not_reused(make_seq):
+    bm = BlockManager(16, BS)
+    a = make_seq(list(range(8)) + [1])
+    _finish_prefill(bm, a)
+    bm.blocks[a.block_table[0]].token_ids = [9, 9, 9, 9]  # stale content behind a matching key
+    assert bm.can_allocate_prefill(make_seq(list(range(8)) + [2]))[0] == 0
+
+
+def test_sharing_a_running_prefix_counts_references(make_seq):
+    bm = BlockManager(16, BS)
+    a = make_seq(list(range(8)) + [1])
+    _finish_prefill(bm, a)
+    b = make_seq(list(range(8)) + [2])
+    assert _finish_prefill(bm, b) == 2
+    shared = a.block_table[:2]
+    assert b.block_table[:2] == shared and all(bm.blocks[i].ref_count == 2 for i in shared)
+    bm.deallocate(a)
+    assert all(bm.blocks[i].ref_count == 1 and i in bm.used_block_ids for i in shared)
+
+
+def test_allocation_reports_a_pool_too_small(make_seq):
+    bm = BlockManager(2, BS)
+    assert bm.can_allocate_prefill(make_seq(range(9)))[0] == -1
+    assert bm.can_allocate_prefill(make_seq(range(8)))[0] == 0
+
+
+def test_reallocating_a_freed_keyed_block_drops_its_key(make_seq):
+    bm = BlockManager(2, BS)
+    a = make_seq(list(range(4)) + [1])
+    _finish_prefill(bm, a)
+    key = bm.blocks[a.block_table[0]].hash
+    assert bm.hash_to_block_id[key] == a.block_table[0]
+    bm.deallocate(a)
+    bm.allocate_block()
+    bm.allocate_block()  # both blocks handed out again: the old key must be gone
+    assert key not in bm.hash_to_block_id
+
+
+def test_decode_takes_a_new_block_only_after_a_boundary(make_seq):
+    bm = BlockManager(8, BS)
+    s = make_seq(range(4))
+    bm.allocate_prefill(s, 0)
+    grown = []
+    for t in range(9):
+        s.append_token(t)
+        before = len(s.block_table)
+        bm.may_append_block(s)
+        grown.append(len(s.block_table) - before)
+    assert grown == [1, 0, 0, 0, 1, 0, 0, 0, 1]  # lengths 5, 9, 13 start a block
+
+
+# ------------------------------------------------------------------ Scheduler
+def _step(sched, token=7):
+    seqs, is_prefill = sched.schedule()
+    sched.postprocess(seqs, [token] * len(seqs), is_prefill)
+    return seqs, is_prefill
+
+
+def test_one_sequence_prefills_then_decodes(make_seq, make_config):
+    sched = Scheduler(make_config())
+    s = make_seq(range(1, 6), max_tokens=3, ignore_eos=True)
+    sched.add(s)
+    assert s.status == SequenceStatus.WAITING
+    seqs, pre = _step(sched)
+    assert pre and seqs == [s] and s.status == SequenceStatus.RUNNING and len(s) == 6
+    seqs, pre = _step(sched)
+    assert not pre and len(s) == 7
+    _step(sched)
+    assert s.status == SequenceStatus.FINISHED and sched.is_finished() and s.block_table == []
+
+
+def test_a_long_prompt_is_chunked_by_the_token_budget(make_seq, make_config):
+    sched = Scheduler(make_config(max_num_batched_tokens=8))
+    s = make_seq(range(1, 21), ignore_eos=True)
+    sched.add(s)
+    sizes = []
+    while True:
+        seqs, pre = sched.schedule()
+        if not pre:
+            break
+        sizes.append(s.num_scheduled_tokens)
+        sched.postprocess(seqs, [7], pre)
+    assert sizes == [8, 8, 4] and len(s) == 21  # one token once the whole prompt is in
+
+
+def test_several_prompts_share_a_prefill_step(make_seq, make_config):
+    sched = Scheduler(make_config())
+    seqs = [make_seq(range(1, 4 + i)) for i in range(3)]
+    for s in seqs:
+        sched.add(s)
+    got, pre = sched.schedule()
+    assert pre and got == seqs
+
+
+def test_max_num_seqs_caps_a_step(make_seq, make_config):
+    sched = Scheduler(make_config(max_num_seqs=2))
+    for i in range(3):
+        sched.add(make_seq(range(1, 5)))
+    got, _ = sched.schedule()
+    assert len(got) == 2
+
+
+def test_a_prompt_that_does_not_fit_waits_for_the_next_step(make_seq, make_config):
+    sched = Scheduler(make_config(max_num_batched_tokens=10))
+    a, b = make_seq(range(1, 7)), make_seq(range(1, 9))
+    sched.add(a)
+    sched.add(b)
+    got, _ = sched.schedule()
+    assert got == [a] and b.block_table == []  # only the first prompt of a step is ever chunked
+
+
+def test_block_exhaustion_preempts_the_newest_running_sequence(make_seq, make_config):
+    sched = Scheduler(make_config(num_kvcache_blocks=4))
+    a, b = make_seq(range(1, 5), ignore_eos=True), make_seq(range(11, 15), ignore_eos=True)
+    sched.add(a)
+    sched.add(b)
+    _step(sched)  # both prefilled: one full block each
+    _step(sched)  # decode: each takes its second block (pool now empty)
+    _step(sched)
+    _step(sched)
+    _step(sched)  # lengths reach 8 (second block full)
+    got, pre = sched.schedule()  # a needs a third block: b is preempted
+    assert not pre and got == [a] and b.status == SequenceStatus.WAITING and b.block_table == []
+    assert sched.waiting[0] is b
+
+
+def test_eos_finishes_a_sequence_unless_ignored(make_seq, make_config):
+    sched = Scheduler(make_config(eos=2))
+    stop, go = make_seq(range(3, 6)), make_seq(range(3, 6), ignore_eos=True)
+    sched.add(stop)
+    sched.add(go)
+    _step(sched, token=2)
+    assert stop.status == SequenceStatus.FINISHED and go.status == SequenceStatus.RUNNING
+
+
+def test_max_tokens_finishes_a_sequence(make_seq, make_config):
+    sched = Scheduler(make_config())
+    s = make_seq(range(3, 6), max_tokens=2, ignore_eos=True)
+    sched.add(s)
+    _step(sched)
+    assert s.status == SequenceStatus.RUNNING
+    _step(sched)
+    assert s.status == SequenceStatus.FINISHED and s.completion_token_ids == [7, 7]

@@ -240,6 +240,10 @@ int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t mu
                     size_t max_bytes, void** comm);
 /* 1 when the communicator has a multicast mapping (switch-reduced modes). */
 int kvb_comm_has_multicast(void* comm);
+/* The exchange kvb_allreduce_add_rmsnorm runs for these arguments (host
+ * only, no device work): plan[0] = 1 for the peer two-shot, plan[1] = 0 (peer
+ * modes), 1 (switch one-shot) or 2 (switch two-shot). */
+int kvb_allreduce_plan(int world, int has_multicast, int tokens, int hidden, int mode, int* plan);
 /* This rank's result rows of the switch two-shot mode: passing them (from row
  * 0) as out / residual_out of kvb_allreduce_add_rmsnorm lets the kernel leave
  * the reduced rows where the switch delivered them instead of copying them

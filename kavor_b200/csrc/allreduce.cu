@@ -400,6 +400,18 @@ cudaError_t launch_w(const ArArgs& a, int blocks, int nch, cudaStream_t st) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Which exchange a call uses (mode 0 = automatic): peer two-shot when the
+// one-shot would read more than 8 MiB per rank; with a multicast mapping and
+// more than two ranks the switch modes instead, two-shot from 8 rows per rank.
+void choose_mode(int world, bool multicast, int tokens, int hidden, int mode, int* two_shot, int* nvls) {
+  const size_t bytes = (size_t)tokens * hidden * 2;
+  *two_shot = world > 2 && (mode == 2 || (mode == 0 && bytes * world > (8u << 20)));
+  if (mode == 2 && world > 1) *two_shot = 1;
+  *nvls = 0;
+  if (mode == 3 || mode == 4) *nvls = mode - 2;
+  if (mode == 0 && multicast && world > 2) *nvls = (size_t)tokens >= (size_t)world * 8 ? 2 : 1;
+}
+
 }  // namespace
 }  // namespace kvb
 
@@ -526,6 +538,13 @@ extern "C" int kvb_comm_result_rows(void* comm, void** out_rows, void** residual
   return kOk;
 }
 
+extern "C" int kvb_allreduce_plan(int world, int has_multicast, int tokens, int hidden, int mode, int* plan) {
+  if (!plan || world < 1 || tokens < 0 || hidden <= 0 || mode < 0 || mode > 4)
+    return set_error(kInvalid, "kvb_allreduce_plan: bad arguments");
+  choose_mode(world, has_multicast != 0, tokens, hidden, mode, &plan[0], &plan[1]);
+  return kOk;
+}
+
 extern "C" int kvb_comm_has_multicast(void* comm) {
   Comm* c = static_cast<Comm*>(comm);
   return c && c->mc ? 1 : 0;
@@ -573,11 +592,7 @@ extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void*
   // full partials per rank, peer two-shot 2 (world - 1) / world of them plus a
   // second flag round; switch one-shot reads one reduced copy, switch
   // two-shot 1/world of it and multicasts 2/world back.
-  a.two_shot = c->world > 2 && (mode == 2 || (mode == 0 && bytes * c->world > (8u << 20)));
-  if (mode == 2 && c->world > 1) a.two_shot = 1;
-  a.nvls = 0;
-  if (mode == 3 || mode == 4) a.nvls = mode - 2;
-  if (mode == 0 && c->mc && c->world > 2) a.nvls = (size_t)tokens >= (size_t)c->world * 8 ? 2 : 1;
+  choose_mode(c->world, c->mc != nullptr, tokens, hidden, mode, &a.two_shot, &a.nvls);
   a.mc_data = c->mc ? reinterpret_cast<const bf16*>(c->mc + L.data[data_index]) : nullptr;
   a.mc_result = c->mc ? reinterpret_cast<bf16*>(c->mc + L.result) : nullptr;
   a.result_stride = ((c->data_bytes + 255) & ~size_t(255)) / 2;

@@ -149,9 +149,9 @@ class TPAllReduce:
         return out, res_out
 
     def switch_two_shot(self, tokens: int, mode: int = 0) -> bool:
-        """The library's automatic choice (and mode 4): reduce 1/W of the rows
-        in the switch and multicast them, from 8 rows per rank up."""
-        return self.multicast and (mode == 4 or (mode == 0 and self.world > 2 and tokens >= 8 * self.world))
+        """Whether the library runs the switch two-shot for this call (its own
+        choice in mode 0, asked through kvb_allreduce_plan)."""
+        return self.multicast and allreduce_plan(self.world, True, tokens, self.hidden, mode)["switch"] == 2
 
     def close(self, group=None) -> None:
         """Collective: every rank's kernels that read this rank's buffers must
@@ -165,6 +165,14 @@ class TPAllReduce:
             self.comm = ctypes.c_void_p()
             self.buffers = []
             self._symm = None
+
+
+def allreduce_plan(world: int, multicast: bool, tokens: int, hidden: int, mode: int = 0) -> dict:
+    """The exchange the fused kernel picks: {"peer_two_shot": 0/1, "switch": 0
+    (peer modes), 1 (switch one-shot) or 2 (switch two-shot)}."""
+    plan = (ctypes.c_int * 2)()
+    _lib.call("kvb_allreduce_plan", world, 1 if multicast else 0, tokens, hidden, mode, plan)
+    return {"peer_two_shot": plan[0], "switch": plan[1]}
 
 
 _TP: TPAllReduce | None = None

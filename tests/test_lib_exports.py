@@ -91,3 +91,25 @@ def test_gemm_plans_are_consistent(lib):
                 assert p["splits"] in (2, 4, 8, 16) and p["grid"] == p["units"]
                 assert (p["splits"] - 1) * math.ceil(kb / p["splits"]) < kb
             assert K.gemm_workspace_bytes(M, N, Kd) == 0  # the split reduces through distributed shared memory
+
+
+def test_allreduce_plan_matches_the_documented_choice(lib):
+    """Host-side mode choice of the fused all-reduce (no launch): peer one-shot
+    at 2 ranks, switch one-shot below 8 rows per rank and switch two-shot from
+    there with a multicast mapping at 4 and 8 ranks, peer two-shot without one
+    when the one-shot would read more than 8 MiB per rank; explicit modes win."""
+    from kavor_b200.layers.allreduce import allreduce_plan
+
+    H = 4096
+    for world in (2, 4, 8):
+        for tokens in (1, 7, 8 * world - 1, 8 * world, 256, 4096):
+            for mc in (False, True):
+                p = allreduce_plan(world, mc, tokens, H)
+                if mc and world > 2:
+                    assert p["switch"] == (2 if tokens >= 8 * world else 1), (world, tokens)
+                else:
+                    assert p["switch"] == 0
+                    assert p["peer_two_shot"] == int(world > 2 and tokens * H * 2 * world > 8 << 20)
+    assert allreduce_plan(2, False, 5, H, mode=2) == {"peer_two_shot": 1, "switch": 0}
+    assert allreduce_plan(8, True, 5, H, mode=4)["switch"] == 2
+    assert allreduce_plan(8, True, 4096, H, mode=1) == {"peer_two_shot": 0, "switch": 0}

@@ -60,23 +60,6 @@ class _Workspace:
 WORKSPACE = _Workspace()
 
 
-class _ZeroedWorkspace(_Workspace):
-    """Like _Workspace but zero-filled at allocation (the GEMM's split-K tickets
-    must start at zero; every GEMM call leaves them at zero)."""
-
-    def reserve(self, nbytes: int, device: torch.device) -> torch.Tensor:
-        idx = device.index if device.index is not None else torch.cuda.current_device()
-        cur = self.buf.get(idx)
-        if cur is not None and cur.numel() >= nbytes:
-            return cur
-        new = super().reserve(nbytes, device)
-        new.zero_()
-        return new
-
-
-GEMM_WORKSPACE = _ZeroedWorkspace()
-
-
 # ------------------------------------------------------------------ KV cache
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   slot_mapping: torch.Tensor) -> None:
@@ -300,11 +283,9 @@ def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
     N = weight.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
-    need = gemm_workspace_bytes(M, N, K, splits)
-    ws = GEMM_WORKSPACE.reserve(need, x.device) if need else None
+    # the K split reduces through distributed shared memory: no workspace
     _lib.call("kvb_gemm_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
-              out.stride(0), M, N, K, splits, ws.data_ptr() if ws is not None else None,
-              ws.numel() if ws is not None else 0, _stream())
+              out.stride(0), M, N, K, splits, None, 0, _stream())
     return out
 
 
@@ -320,12 +301,8 @@ def gemm_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = 
     inter = weight.shape[0] // 2
     if out is None:
         out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
-    n = ctypes.c_size_t(0)
-    _lib.call("kvb_gemm_silu_workspace_size", M, inter, K, splits, ctypes.byref(n))
-    ws = GEMM_WORKSPACE.reserve(int(n.value), x.device) if n.value else None
     _lib.call("kvb_gemm_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
-              out.stride(0), M, inter, K, splits, ws.data_ptr() if ws is not None else None,
-              ws.numel() if ws is not None else 0, _stream())
+              out.stride(0), M, inter, K, splits, None, 0, _stream())
     return out
 
 

@@ -1,4 +1,4 @@
-"""Decode-step benchmark of the kavor_b200 Qwen3 path (BASELINE config 3 headline).
+"""Decode-step benchmark of the kavor_b200 Qwen3 path (Qwen3-8B decode, the headline metric).
 
 Workload: Qwen3-8B (random-init bf16, the reference checkpoint shapes), a
 decode batch of 256 sequences whose context is 1024 tokens (block_size 256),

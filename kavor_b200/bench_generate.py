@@ -1,5 +1,5 @@
-"""Offline generate throughput through the public API (the
-workload of the reference's own benchmark, benchs/bench.py:8-26).
+"""Offline generate throughput through the public API, on the workload of the
+reference's own benchmark (benchs/bench.py:8-26).
 
     python -m kavor_b200.bench_generate [--model Qwen3-0.6B] [--tp 1] [--num-seqs 256]
 

@@ -51,7 +51,7 @@ struct Comm {
   uint8_t* peer[kMaxRanks] = {};
   uint8_t* mc = nullptr;    // NVLink multicast mapping of the area (NULL: none)
   uint32_t* counters = nullptr;     // [kMaxBlocks] calls per block (peer flag rounds)
-  uint32_t* mc_counters = nullptr;  // [2][kMaxBlocks] calls per block that ran switch round 0 / round 1
+  uint32_t* mc_counters = nullptr;  // [2][kMaxBlocks] calls per block that ran the first / second switch arrival
   bool opened[kMaxRanks] = {};
   bool owns_area = true;    // false: the area was attached (allocated and mapped by the caller)
 };

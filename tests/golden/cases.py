@@ -2,7 +2,7 @@
 
 Every case is rebuilt from its seed on demand (CPU generators are
 deterministic for a given torch build), so the committed fixtures only hold
-outputs and small metadata. Shapes follow BASELINE configs 1 and 3:
+outputs and small metadata. Shapes follow the one-layer case and the 8B decode case:
 Qwen3-0.6B / Qwen3-8B layer shapes, head_dim 128, block_size 256, context
 lengths U[100, 1024] from seed 0, KV pages N(0, 1), block tables a random
 permutation of the pool's blocks.
@@ -70,7 +70,7 @@ def decode_batch(batch: int, lo: int, hi: int, block_size: int, seed: int, spare
 
 
 def config1_layer_case(seed: int = 0) -> dict:
-    """one Qwen3-0.6B decoder layer, one decode step, B = 16."""
+    """The one-layer case: one Qwen3-0.6B decoder layer, one decode step, B = 16."""
     shape = QWEN3_06B
     hd, hkv = shape["head_dim"], shape["num_key_value_heads"]
     ctx, tables, nblk, pos, slots = decode_batch(16, 100, 1024, 256, seed)

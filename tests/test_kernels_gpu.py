@@ -1,8 +1,8 @@
 """Kernel parity: every sm_100a kernel of libkavor_b200.so against the CPU oracle
 on seeded inputs. Integer/byte work (KV write, embedding, residual, greedy
 argmax) must be bit-exact; floating-point outputs use the reference suite's
-tolerances (tests/test_fused_kernels.py there: 2e-2) or the north-star
-per-layer bound (max-abs 2e-2, rel 1e-2)."""
+tolerances (tests/test_fused_kernels.py there: 2e-2) or the per-layer
+parity bound (max-abs 2e-2, rel 1e-2)."""
 import pytest
 import torch
 
@@ -178,7 +178,7 @@ def _decode_case(B, hq, hkv, ctx, seed, nan_tail=False):
 
 
 @pytest.mark.parametrize("B,hq,hkv,ctx,splits", [
-    (16, 16, 8, None, 0),                    # BASELINE config 1 batch (0.6B heads, ctx U[100,1024])
+    (16, 16, 8, None, 0),                    # the one-layer case batch (0.6B heads, ctx U[100,1024])
     (4, 32, 8, [1, 63, 64, 65], 0),          # tile-boundary contexts
     (3, 4, 1, [1024, 1000, 257], 0),         # TP8-like: 1 kv head, group 4
     (2, 64, 8, [700, 1500], 0),              # group 8 (Qwen3-32B TP1)

@@ -37,8 +37,8 @@ def _load(module, tensors, packed):
 
 
 def test_config1_decoder_layer_matches_reference():
-    """BASELINE config 1 (one Qwen3-0.6B layer, one decode step, B=16) vs the
-    reference layer's output: max-abs 2e-2 / rel 1e-2."""
+    """One Qwen3-0.6B layer, one decode step, B=16, vs the reference layer's
+    output: max-abs 2e-2 / rel 1e-2 (the per-layer parity bound)."""
     from kavor_b200.models.qwen3 import Qwen3DecoderLayer, Qwen3ForCausalLM
     from kavor_b200.utils.context import reset_context, set_context
 

@@ -69,7 +69,7 @@ def _oracle_layer(case, residual):
 
 
 def test_decoder_layer_matches_reference_layer():
-    """one 0.6B decoder layer, one decode step, B=16."""
+    """The one-layer case: one 0.6B decoder layer, one decode step, B=16."""
     case = cases.config1_layer_case(0)
     gold = _load("layer_golden.pt")
     for variant, res in (("first", None), ("later", case["residual"].clone())):

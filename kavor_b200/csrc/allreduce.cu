@@ -147,9 +147,11 @@ __device__ bool flag_round(const ArArgs& a, int phase, uint32_t v, bool publish,
   __syncthreads();
   if (threadIdx.x < W) {
     const uint32_t* f = a.flags[a.rank] + ((size_t)phase * kMaxBlocks + b) * kMaxRanks + threadIdx.x;
-    if (ld_acquire(f) != v) {
+    // flags only grow (each is the peer's call count), so "at least v" also
+    // holds when a fast peer has already moved on to its next call
+    if ((int)(ld_acquire(f) - v) < 0) {
       const long long t0 = clock64();
-      while (ld_acquire(f) != v) {
+      while ((int)(ld_acquire(f) - v) < 0) {
         if (clock64() - t0 > kSpinCycles) {
           atomicOr(&g_err_allreduce, (unsigned)kErrPeerTimeout);
           *ok_s = 0;

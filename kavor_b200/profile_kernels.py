@@ -112,8 +112,6 @@ def _sample(a, dev):
 
 
 def _gemm(a, dev, use_torch=False):
-    import torch.nn.functional as F
-
     M, N, K_ = a.batch, a.inter, a.hidden
     xs = [torch.randn(M, K_, device=dev).to(torch.bfloat16) for _ in range(a.copies)]
     ws = [(torch.randn(N, K_, device=dev) * 0.02).to(torch.bfloat16) for _ in range(a.copies)]

@@ -4,7 +4,6 @@
 ``-m "not gpu"`` tests run on any CPU (oracle vs golden fixtures, host-side
 scheduling and metadata, library exports, gloo multi-rank logic).
 """
-import os
 import sys
 from pathlib import Path
 

@@ -15,7 +15,9 @@ What runs is the reference's own code on the CPU:
   the reference's TP layers and weight loaders on a 1-rank gloo group. Its
   three non-CPU kernels are replaced: the Triton RoPE by the eager function
   above, store_kvcache (Triton) and the two flash_attn calls by oracle.ops
-  (flash-attn is a third-party wheel; that boundary stays parity-unpinned);
+  (flash-attn is a third-party GPU wheel; that boundary is pinned on the GPU
+  instead, by running the wheel beside the kernels:
+  tests/test_flash_attn_parity_gpu.py);
 * Scheduler + BlockManager + ModelRunner.prepare_prefill/prepare_decode
   (scheduler.py, block_manager.py, model_runner.py:385-473) on a scripted
   request stream, with the CUDA uploads turned into CPU no-ops.

@@ -22,7 +22,8 @@ What runs is the reference's own code on the CPU:
   (scheduler.py, block_manager.py, model_runner.py:385-473) on a scripted
   request stream, with the CUDA uploads turned into CPU no-ops.
 
-Outputs: ops_golden.pt, layer_golden.pt, tiny_model_golden.pt, host_trace.json.
+Outputs: ops_golden.pt, layer_golden.pt, tiny_model_golden.pt, tiny_model_golden_32.pt,
+host_trace.json.
 """
 from __future__ import annotations
 
@@ -169,9 +170,12 @@ def golden_layer() -> dict:
     return res
 
 
-def golden_tiny_model() -> dict:
+def golden_tiny_model(decode_steps: int = 8, keep_logits: bool = True) -> dict:
     """Greedy generation of a 2-layer Qwen3 (reference model class, CPU) for 3
-    prompts: one prefill step then 8 decode steps, block_size 256."""
+    prompts: one prefill step then `decode_steps` decode steps, block_size 256.
+    Every step keeps its tokens and the gap between the two largest logits of
+    each row (a near-tie there is where a bf16 rounding difference may pick
+    the other token); the logits themselves only with keep_logits."""
     from kavor.models.qwen3 import Qwen3ForCausalLM
     from kavor.utils.context import reset_context, set_context
 
@@ -213,11 +217,10 @@ def golden_tiny_model() -> dict:
         set_context(True, cu, cu, max(map(len, seqs)), max(map(len, seqs)), slots, None, None)
         logits = model.compute_logits(model(ids, pos))
         reset_context()
-        tok = logits.float().argmax(-1).tolist()
-        steps.append(dict(logits=logits.clone(), tokens=tok))
-        for b, t in enumerate(tok):
+        steps.append(_step_record(logits, keep_logits))
+        for b, t in enumerate(steps[-1]["tokens"]):
             seqs[b].append(t)
-        for _ in range(8):
+        for _ in range(decode_steps):
             ids = torch.tensor([p[-1] for p in seqs])
             pos = torch.tensor([len(p) - 1 for p in seqs])
             ctx = torch.tensor([len(p) for p in seqs], dtype=torch.int32)
@@ -225,11 +228,18 @@ def golden_tiny_model() -> dict:
             set_context(False, slot_mapping=slots, context_lens=ctx, block_tables=torch.tensor(tables, dtype=torch.int32))
             logits = model.compute_logits(model(ids, pos))
             reset_context()
-            tok = logits.float().argmax(-1).tolist()
-            steps.append(dict(logits=logits.clone(), tokens=tok))
-            for b, t in enumerate(tok):
+            steps.append(_step_record(logits, keep_logits))
+            for b, t in enumerate(steps[-1]["tokens"]):
                 seqs[b].append(t)
     return dict(prompts=prompts, tables=tables, steps=steps)
+
+
+def _step_record(logits: torch.Tensor, keep_logits: bool) -> dict:
+    top2 = logits.float().topk(2, dim=-1).values
+    rec = dict(tokens=logits.float().argmax(-1).tolist(), margins=(top2[:, 0] - top2[:, 1]).tolist())
+    if keep_logits:
+        rec["logits"] = logits.clone()
+    return rec
 
 
 def golden_host_trace() -> dict:
@@ -308,6 +318,7 @@ def main() -> int:
     torch.save(golden_ops(), out / "ops_golden.pt")
     torch.save(golden_layer(), out / "layer_golden.pt")
     torch.save(golden_tiny_model(), out / "tiny_model_golden.pt")
+    torch.save(golden_tiny_model(decode_steps=31, keep_logits=False), out / "tiny_model_golden_32.pt")
     (out / "host_trace.json").write_text(json.dumps(golden_host_trace()))
     dist.destroy_process_group()
     for f in sorted(out.glob("*golden*")) + [out / "host_trace.json"]:

@@ -106,6 +106,45 @@ def test_tiny_model_greedy_matches_reference_model():
         _, logits = omodel.forward(p, ids, batch, kv, shape)
 
 
+def test_tiny_model_32_greedy_tokens_match_reference_model():
+    """32 greedy tokens (prefill + 31 decode steps) of the reference model
+    class, teacher-forced: at every step the oracle is fed the reference's
+    token, and its own argmax must equal it wherever the reference's two
+    largest logits are more than two bf16 ulps apart (2 x 2^-7 at the |logit| <
+    2 of this random-init model, whose logits are flat enough to come within
+    an ulp of each other at a few steps: there the order is decided by the
+    last rounding of a 512-term dot product, not by the algorithm)."""
+    gold = _load("tiny_model_golden_32.pt")
+    shape = omodel.Shape(hidden=512, inter=1024, layers=2, hq=4, hkv=2, vocab=4096)
+    p = cases.checkpoint(cases.TINY, seed=5)
+    kv = [(torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16), torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16))
+          for _ in range(2)]
+    seqs = [list(x) for x in gold["prompts"]]
+    tables = gold["tables"]
+    ids = torch.tensor([t for s in seqs for t in s])
+    pos = torch.tensor([i for s in seqs for i in range(len(s))])
+    cu = torch.tensor([0] + list(torch.tensor([len(s) for s in seqs]).cumsum(0)), dtype=torch.int32)
+    slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))])
+    _, logits = omodel.forward(p, ids, omodel.Batch(True, pos, slots, cu, cu), kv, shape)
+    assert len(gold["steps"]) == 32
+    checked = 0
+    for step in gold["steps"]:
+        tok = logits.float().argmax(-1).tolist()
+        for b, (mine, ref, margin) in enumerate(zip(tok, step["tokens"], step["margins"])):
+            if margin > 2 * 2.0 ** -7:
+                assert mine == ref, (b, mine, ref, margin)
+                checked += 1
+        for b, t in enumerate(step["tokens"]):  # teacher forcing
+            seqs[b].append(t)
+        ids = torch.tensor([s[-1] for s in seqs])
+        pos = torch.tensor([len(s) - 1 for s in seqs])
+        ctx = torch.tensor([len(s) for s in seqs], dtype=torch.int32)
+        slots = torch.tensor([tables[b][0] * 256 + len(s) - 1 for b, s in enumerate(seqs)])
+        batch = omodel.Batch(False, pos, slots, context_lens=ctx, block_tables=torch.tensor(tables, dtype=torch.int32))
+        _, logits = omodel.forward(p, ids, batch, kv, shape)
+    assert checked >= 84  # of 96 (3 sequences x 32 tokens)
+
+
 def test_philox_known_answer():
     """Philox4x32-10 known-answer vectors of the Random123 distribution
     (kat_vectors: counter 0, key 0 and counter/key all-ones)."""

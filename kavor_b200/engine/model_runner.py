@@ -371,7 +371,6 @@ class ModelRunner:
         self.model.lm_head.sample(hidden, d["temperatures"][:bs], self.sampler.seed,
                                   out=self.decode_buffers.sampled[:bs])
 
-    @torch.inference_mode()
     def _sync_ranks(self) -> None:
         """Before a forward that runs the fused all-reduce during set-up: the
         ranks' host work so far differs, and the kernel's peer wait is bounded."""
@@ -379,6 +378,7 @@ class ModelRunner:
             torch.cuda.synchronize(self.device)
             dist.barrier()
 
+    @torch.inference_mode()
     def capture_cudagraph(self) -> None:
         max_bs = self._max_graph_bs()
         self.decode_buffers = DecodeBuffers(max_bs, self.max_blocks_per_seq, self.device)

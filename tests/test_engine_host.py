@@ -237,3 +237,14 @@ def test_max_tokens_finishes_a_sequence(make_seq, make_config):
     assert s.status == SequenceStatus.RUNNING
     _step(sched)
     assert s.status == SequenceStatus.FINISHED and s.completion_token_ids == [7, 7]
+
+
+# ------------------------------------------------------------------ ModelRunner
+def test_runner_forwards_run_under_inference_mode():
+    """Every ModelRunner method that runs the model (set-up forwards, graph
+    capture, the step) is wrapped in torch.inference_mode: the buffers these
+    create are inference tensors, and an in-place update of one outside
+    inference mode (the sampler seed restore after capture) raises."""
+    from kavor_b200.engine.model_runner import ModelRunner
+    for name in ("_profile_prefill", "_profile_decode", "capture_cudagraph", "run"):
+        assert hasattr(getattr(ModelRunner, name), "__wrapped__"), name

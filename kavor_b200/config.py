@@ -24,7 +24,7 @@ def free_port() -> int:
 
 
 def load_hf_config(model_dir: str):
-    """Text config of a Qwen3-family model directory (transformers' own parser)."""
+    """Text config of a model directory (transformers' own parser)."""
     from transformers import AutoConfig
 
     return AutoConfig.from_pretrained(model_dir, trust_remote_code=False)
@@ -78,13 +78,30 @@ QWEN3_PRESETS: dict[str, dict] = {
                       num_key_value_heads=8, head_dim=128, tie_word_embeddings=False),
 }
 
+# The other dense families the model registry serves, one published size each.
+FAMILY_PRESETS: dict[str, dict] = {
+    "Mistral-7B-v0.3": dict(architectures=["MistralForCausalLM"], model_type="mistral", vocab_size=32768,
+                            hidden_size=4096, intermediate_size=14336, num_hidden_layers=32, num_attention_heads=32,
+                            num_key_value_heads=8, head_dim=128, max_position_embeddings=32768, rms_norm_eps=1e-5,
+                            rope_theta=1000000.0, hidden_act="silu", sliding_window=None, tie_word_embeddings=False,
+                            torch_dtype="bfloat16", bos_token_id=1, eos_token_id=2),
+    "ERNIE-4.5-0.3B": dict(architectures=["Ernie4_5ForCausalLM"], model_type="ernie4_5", vocab_size=103424,
+                           hidden_size=1024, intermediate_size=3072, num_hidden_layers=18, num_attention_heads=16,
+                           num_key_value_heads=2, head_dim=128, max_position_embeddings=131072, rms_norm_eps=1e-5,
+                           rope_theta=500000.0, hidden_act="silu", use_bias=False, tie_word_embeddings=True,
+                           torch_dtype="bfloat16", bos_token_id=1, eos_token_id=2),
+}
+
 
 def write_model_dir(path: str, preset: str, **overrides) -> str:
     """Write a weight-less model directory (config.json only) for load_format='dummy'."""
-    cfg = dict(architectures=["Qwen3ForCausalLM"], model_type="qwen3", vocab_size=151936,
-               max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1000000.0, hidden_act="silu",
-               attention_bias=False, torch_dtype="bfloat16", bos_token_id=151643, eos_token_id=151645)
-    cfg.update(QWEN3_PRESETS[preset])
+    if preset in FAMILY_PRESETS:
+        cfg = dict(FAMILY_PRESETS[preset])
+    else:
+        cfg = dict(architectures=["Qwen3ForCausalLM"], model_type="qwen3", vocab_size=151936,
+                   max_position_embeddings=40960, rms_norm_eps=1e-6, rope_theta=1000000.0, hidden_act="silu",
+                   attention_bias=False, torch_dtype="bfloat16", bos_token_id=151643, eos_token_id=151645)
+        cfg.update(QWEN3_PRESETS[preset])
     cfg.update(overrides)
     os.makedirs(path, exist_ok=True)
     with open(os.path.join(path, "config.json"), "w") as f:

@@ -10,8 +10,9 @@ parameters through the per-parameter ``weight_loader`` of the TP layers:
 * ``load_format="dummy"``: a synthetic checkpoint with the reference
   checkpoint's tensor names and FULL (unsharded) shapes, every tensor drawn on
   the target device from its own seeded generator: matrices N(0, 0.02), norm
-  gains N(1, 0.1). Because it goes through the same TP loaders, a TP=N model
-  is exactly the TP=1 model sharded.
+  gains N(1, 0.1), projection biases N(0, 0.5) (the size of the projections'
+  outputs, so a bias visibly moves them). Because it goes through the same TP
+  loaders, a TP=N model is exactly the TP=1 model sharded.
 """
 from __future__ import annotations
 
@@ -22,9 +23,16 @@ import zlib
 import torch
 from torch import nn
 
+from kavor_b200.models.ernie4_5 import Ernie4_5ForCausalLM
+from kavor_b200.models.mistral import MistralForCausalLM
 from kavor_b200.models.qwen3 import Qwen3ForCausalLM
 
-MODEL_REGISTRY: dict[str, type[nn.Module]] = {"qwen3": Qwen3ForCausalLM}
+# model_type -> class (model_mapping.py:6-15, the dense text families)
+MODEL_REGISTRY: dict[str, type[nn.Module]] = {
+    "qwen3": Qwen3ForCausalLM,
+    "mistral": MistralForCausalLM,
+    "ernie4_5": Ernie4_5ForCausalLM,
+}
 
 
 def _assign(model: nn.Module, name: str, tensor: torch.Tensor, packed: dict, loaded: set[str]) -> None:
@@ -45,7 +53,11 @@ def _assign(model: nn.Module, name: str, tensor: torch.Tensor, packed: dict, loa
 
 
 def synthetic_checkpoint(config, seed: int, device: torch.device):
-    """Yield (name, full tensor) of a Qwen3 checkpoint with random values."""
+    """Yield (name, full tensor) of a checkpoint of the config's model family
+    (q/k norm gains or q/k/v biases as that family's attention has them) with
+    random values."""
+    layout = AutoModelForCausalLM.model_class(config).attention_layout(config)
+    tie = AutoModelForCausalLM.model_class(config).ties_word_embeddings(config)
     H, I = config.hidden_size, config.intermediate_size
     hd = getattr(config, "head_dim", None) or H // config.num_attention_heads
     Hq, Hkv = config.num_attention_heads, config.num_key_value_heads
@@ -65,17 +77,17 @@ def synthetic_checkpoint(config, seed: int, device: torch.device):
                          ("mlp.gate_proj.weight", (I, H)), ("mlp.up_proj.weight", (I, H)),
                          ("mlp.down_proj.weight", (H, I))):
             yield p + n, draw(p + n, shape, 0.0, 0.02)
-        if not getattr(config, "attention_bias", True):
+        if layout["qk_norm"]:
             for n in ("self_attn.q_norm.weight", "self_attn.k_norm.weight"):
                 yield p + n, draw(p + n, (hd,), 1.0, 0.1)
-        else:
+        if layout["qkv_bias"]:
             for n, size in (("self_attn.q_proj.bias", Hq * hd), ("self_attn.k_proj.bias", Hkv * hd),
                             ("self_attn.v_proj.bias", Hkv * hd)):
-                yield p + n, draw(p + n, (size,), 0.0, 0.02)
+                yield p + n, draw(p + n, (size,), 0.0, 0.5)
         for n in ("input_layernorm.weight", "post_attention_layernorm.weight"):
             yield p + n, draw(p + n, (H,), 1.0, 0.1)
     yield "model.norm.weight", draw("model.norm.weight", (H,), 1.0, 0.1)
-    if not getattr(config, "tie_word_embeddings", False):
+    if not tie:
         yield "lm_head.weight", draw("lm_head.weight", (config.vocab_size, H), 0.0, 0.02)
 
 
@@ -128,7 +140,7 @@ class AutoModelForCausalLM:
         for name, tensor in source:
             _assign(model, name, tensor, packed, loaded)
         params = {n for n, _ in model.named_parameters()}
-        if getattr(hf_config, "tie_word_embeddings", False):
+        if model.ties_word_embeddings(hf_config):
             loaded.add("lm_head.weight")
         missing = sorted(params - loaded)
         if missing:

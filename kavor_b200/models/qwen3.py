@@ -42,7 +42,8 @@ class Qwen3Attention(nn.Module):
 
     def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, max_position: int = 4096 * 32,
                  head_dim: int | None = None, rms_norm_eps: float = 1e-06, qkv_bias: bool = False,
-                 rope_theta: float = 10000, rope_scaling: dict | None = None) -> None:
+                 rope_theta: float = 10000, rope_scaling: dict | None = None, qk_norm: bool | None = None,
+                 rope_interleaved: bool = False) -> None:
         super().__init__()
         _, tp_size = _tp()
         if num_heads % tp_size or num_kv_heads % tp_size:
@@ -56,6 +57,9 @@ class Qwen3Attention(nn.Module):
         self.kv_size = self.num_kv_heads * self.head_dim
         self.scaling = self.head_dim ** -0.5
         self.qkv_bias = qkv_bias
+        # Qwen3 normalises q and k exactly when the projection has no bias
+        # (qwen3.py:71-73, :136); the other dense families choose explicitly
+        self.qk_norm = (not qkv_bias) if qk_norm is None else qk_norm
         self.rms_norm_eps = rms_norm_eps
         self.qkv_proj = QKVParallelLinear((num_heads + 2 * num_kv_heads) * self.head_dim, hidden_size,
                                           self.head_dim, num_heads, num_kv_heads, bias=qkv_bias)
@@ -63,9 +67,9 @@ class Qwen3Attention(nn.Module):
         if isinstance(rope_scaling, dict):
             rope_theta = rope_scaling.get("rope_theta", rope_theta)
         self.rotary_emb = get_rope(self.head_dim, rotary_dim=self.head_dim, max_position=max_position,
-                                   base=rope_theta)
+                                   base=rope_theta, interleaved=rope_interleaved)
         self.attn = Attention(self.num_heads, self.head_dim, self.scaling, self.num_kv_heads)
-        if not qkv_bias:
+        if self.qk_norm:
             self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
             self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
 
@@ -77,7 +81,7 @@ class Qwen3Attention(nn.Module):
         has_cache = k_cache.numel() > 0
         K.qknorm_rope_store(
             qkv, self.num_heads, self.num_kv_heads, self.head_dim,
-            None if self.qkv_bias else self.q_norm.weight, None if self.qkv_bias else self.k_norm.weight,
+            self.q_norm.weight if self.qk_norm else None, self.k_norm.weight if self.qk_norm else None,
             self.rms_norm_eps, positions, self.rotary_emb.cos_sin_cache, self.rotary_emb.interleaved,
             k_cache if has_cache else None, v_cache if has_cache else None,
             ctx.slot_mapping if has_cache else None)
@@ -107,7 +111,15 @@ class Qwen3DecoderLayer(nn.Module):
 
     def __init__(self, config) -> None:
         super().__init__()
-        self.self_attn = Qwen3Attention(
+        self.self_attn = self.make_attention(config)
+        self.mlp = Qwen3MLP(config.hidden_size, config.intermediate_size, config.hidden_act)
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    @staticmethod
+    def make_attention(config) -> Qwen3Attention:
+        """qwen3.py:130-140."""
+        return Qwen3Attention(
             hidden_size=config.hidden_size,
             num_heads=config.num_attention_heads,
             num_kv_heads=config.num_key_value_heads,
@@ -118,9 +130,12 @@ class Qwen3DecoderLayer(nn.Module):
             rope_theta=rope_theta_of(config),
             rope_scaling=None,
         )
-        self.mlp = Qwen3MLP(config.hidden_size, config.intermediate_size, config.hidden_act)
-        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
-        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+
+    @staticmethod
+    def attention_layout(config) -> dict:
+        """Which optional attention tensors the checkpoint holds."""
+        bias = getattr(config, "attention_bias", True)
+        return dict(qk_norm=not bias, qkv_bias=bias)
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor,
                 residual: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -135,11 +150,12 @@ class Qwen3DecoderLayer(nn.Module):
 
 
 class Qwen3Model(nn.Module):
+    layer_cls = Qwen3DecoderLayer
 
     def __init__(self, config) -> None:
         super().__init__()
         self.embed_tokens = VocabParallelEmbedding(config.vocab_size, config.hidden_size)
-        self.layers = nn.ModuleList([Qwen3DecoderLayer(config) for _ in range(config.num_hidden_layers)])
+        self.layers = nn.ModuleList([self.layer_cls(config) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
@@ -184,12 +200,23 @@ class Qwen3ForCausalLM(nn.Module):
         "up_proj": ("gate_up_proj", 1),
     }
 
+    model_cls = Qwen3Model
+
     def __init__(self, config) -> None:
         super().__init__()
-        self.model = Qwen3Model(config)
+        self.model = self.model_cls(config)
         self.lm_head = ParallelLMHead(config.vocab_size, config.hidden_size)
-        if getattr(config, "tie_word_embeddings", False):
+        if self.ties_word_embeddings(config):
             self.lm_head.weight.data = self.model.embed_tokens.weight.data
+
+    @staticmethod
+    def ties_word_embeddings(config) -> bool:
+        """qwen3.py:205-206: the LM head shares the embedding when the config says so."""
+        return bool(getattr(config, "tie_word_embeddings", False))
+
+    @classmethod
+    def attention_layout(cls, config) -> dict:
+        return cls.model_cls.layer_cls.attention_layout(config)
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         return self.model(input_ids, positions)

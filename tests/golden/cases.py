@@ -33,6 +33,44 @@ def hf_config(shape: dict, **over):
     return cfg
 
 
+# Tiny members of the other dense families (2 layers, TINY shapes, untied LM
+# head: a tied head on random weights repeats the prompt's last token). Mistral:
+# no q/k norm, no bias, rope theta 1e4; ERNIE 4.5: q/k/v bias, interleaved
+# RoPE, theta 5e5. Both with eps 1e-5 (their published configs').
+FAMILIES = ("mistral", "ernie4_5")
+
+
+def family_config(family: str):
+    from transformers import Ernie4_5Config, MistralConfig
+
+    kw = dict(TINY, max_position_embeddings=4096, rms_norm_eps=1e-5, hidden_act="silu")
+    if family == "mistral":
+        return MistralConfig(**kw, rope_theta=10000.0)
+    if family == "ernie4_5":
+        kw.update(use_bias=True)
+        return Ernie4_5Config(**kw, rope_theta=500000.0)
+    raise ValueError(family)
+
+
+def family_checkpoint(family: str, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Full checkpoint of the tiny family model drawn by kavor_b200's dummy loader."""
+    from kavor_b200.models import synthetic_checkpoint
+
+    return dict(synthetic_checkpoint(family_config(family), seed, torch.device("cpu")))
+
+
+def family_oracle_shape(family: str):
+    from oracle import model as omodel
+
+    cfg = family_config(family)
+    theta = cfg.rope_parameters["rope_theta"]
+    return omodel.Shape(hidden=cfg.hidden_size, inter=cfg.intermediate_size, layers=cfg.num_hidden_layers,
+                        hq=cfg.num_attention_heads, hkv=cfg.num_key_value_heads, vocab=cfg.vocab_size,
+                        eps=cfg.rms_norm_eps, rope_theta=theta, tie=False,
+                        qk_norm=False, qkv_bias=family == "ernie4_5", interleaved=family == "ernie4_5",
+                        separate_residual_add=family == "ernie4_5")
+
+
 def checkpoint(shape: dict, seed: int = 0, layers: int | None = None) -> dict[str, torch.Tensor]:
     """Full (TP=1) checkpoint tensors drawn on the CPU by kavor_b200's dummy loader."""
     from kavor_b200.models import synthetic_checkpoint
@@ -144,3 +182,50 @@ def run_host_trace(make_seq, scheduler, meta_prefill, meta_decode, max_steps: in
         trace.append({"step": step, "prefill": bool(is_prefill), "reqs": reqs, "tokens": tokens,
                       "meta": {k: _plain(v) for k, v in meta.items()}})
     return trace, {r: list(s.completion_token_ids) for r, s in seqs.items()}
+
+
+def replay(gold: dict, run_step):
+    """Teacher-forced replay of a greedy fixture (make_golden._greedy_run):
+    yields (logits, step record) for the prefill and every decode step, and
+    then appends the REFERENCE's tokens, so one near-tie cannot derail the
+    rest. ``run_step(batch)`` returns the [B, vocab] logits of a step; the
+    batch dict holds CPU tensors: is_prefill, input_ids, positions,
+    slot_mapping (int32), and cu_seqlens (int32) for the prefill or
+    context_lens / block_tables (int32) for a decode step. Block size 256,
+    one block per sequence (gold["tables"])."""
+    seqs = [list(p) for p in gold["prompts"]]
+    tables = gold["tables"]
+    i32 = torch.int32
+    batch = dict(is_prefill=True,
+                 input_ids=torch.tensor([t for s in seqs for t in s]),
+                 positions=torch.tensor([i for s in seqs for i in range(len(s))]),
+                 cu_seqlens=torch.tensor([0] + torch.tensor([len(s) for s in seqs]).cumsum(0).tolist(), dtype=i32),
+                 slot_mapping=torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))],
+                                           dtype=i32))
+    for step in gold["steps"]:
+        yield run_step(batch), step
+        for b, t in enumerate(step["tokens"]):
+            seqs[b].append(t)
+        batch = dict(is_prefill=False,
+                     input_ids=torch.tensor([s[-1] for s in seqs]),
+                     positions=torch.tensor([len(s) - 1 for s in seqs]),
+                     slot_mapping=torch.tensor([tables[b][0] * 256 + len(s) - 1 for b, s in enumerate(seqs)], dtype=i32),
+                     context_lens=torch.tensor([len(s) for s in seqs], dtype=i32),
+                     block_tables=torch.tensor(tables, dtype=i32))
+
+
+def check_greedy_step(logits: torch.Tensor, step: dict, min_cos: float = 0.999, ulps: int = 2) -> int:
+    """Logits cosine >= min_cos against the reference's row by row, and the
+    argmax equal to the reference's token wherever the reference's two largest
+    logits are more than `ulps` bf16 ulps (2^-7 each at |logit| < 2) apart.
+    Returns the number of tokens compared."""
+    logits = logits.float().cpu()
+    if "logits" in step:
+        cos = torch.nn.functional.cosine_similarity(logits, step["logits"].float(), dim=-1)
+        assert cos.min().item() >= min_cos, cos
+    checked = 0
+    for b, (mine, ref, margin) in enumerate(zip(logits.argmax(-1).tolist(), step["tokens"], step["margins"])):
+        if margin > ulps * 2.0 ** -7:
+            assert mine == ref, (b, mine, ref, margin)
+            checked += 1
+    return checked

@@ -20,10 +20,12 @@ What runs is the reference's own code on the CPU:
   tests/test_flash_attn_parity_gpu.py);
 * Scheduler + BlockManager + ModelRunner.prepare_prefill/prepare_decode
   (scheduler.py, block_manager.py, model_runner.py:385-473) on a scripted
-  request stream, with the CUDA uploads turned into CPU no-ops.
+  request stream, with the CUDA uploads turned into CPU no-ops;
+* MistralForCausalLM and Ernie4_5ForCausalLM (mistral.py, ernie4_5.py) on
+  tiny configs, the same greedy run as the Qwen3 model.
 
 Outputs: ops_golden.pt, layer_golden.pt, tiny_model_golden.pt, tiny_model_golden_32.pt,
-host_trace.json.
+mistral_tiny_golden.pt, ernie4_5_tiny_golden.pt, host_trace.json.
 """
 from __future__ import annotations
 
@@ -177,17 +179,31 @@ def golden_tiny_model(decode_steps: int = 8, keep_logits: bool = True) -> dict:
     each row (a near-tie there is where a bf16 rounding difference may pick
     the other token); the logits themselves only with keep_logits."""
     from kavor.models.qwen3 import Qwen3ForCausalLM
-    from kavor.utils.context import reset_context, set_context
 
     shape = cases.TINY
-    cfg = cases.hf_config(shape)
+    model = _ref_model(Qwen3ForCausalLM, cases.hf_config(shape), cases.checkpoint(shape, seed=5))
+    return _greedy_run(model, shape["num_key_value_heads"], decode_steps, keep_logits)
+
+
+def golden_family_model(family: str, decode_steps: int = 8) -> dict:
+    """The same greedy run on the tiny member of another dense family
+    (reference classes mistral.py:147-175 / ernie4_5.py:180-209)."""
+    from kavor.models.ernie4_5 import Ernie4_5ForCausalLM
+    from kavor.models.mistral import MistralForCausalLM
+
+    cls = {"mistral": MistralForCausalLM, "ernie4_5": Ernie4_5ForCausalLM}[family]
+    cfg = cases.family_config(family)
+    model = _ref_model(cls, cfg, cases.family_checkpoint(family, seed=5))
+    return _greedy_run(model, cfg.num_key_value_heads, decode_steps, True)
+
+
+def _ref_model(cls, cfg, ckpt: dict):
     torch.set_default_dtype(torch.bfloat16)
     try:
-        model = Qwen3ForCausalLM(cfg)
+        model = cls(cfg)
     finally:
         torch.set_default_dtype(torch.float32)
-    ckpt = cases.checkpoint(shape, seed=5)
-    packed = Qwen3ForCausalLM.packed_modules_mapping
+    packed = cls.packed_modules_mapping
     for name, t in ckpt.items():
         for k, (v, sid) in packed.items():
             if k in name:
@@ -198,9 +214,14 @@ def golden_tiny_model(decode_steps: int = 8, keep_logits: bool = True) -> dict:
             p = model.get_parameter(name)
             loader = getattr(p, "weight_loader", None)
             p.data.copy_(t) if loader is None else loader(p, t)
-    hkv = shape["num_key_value_heads"]
+    return model
+
+
+def _greedy_run(model, hkv: int, decode_steps: int, keep_logits: bool) -> dict:
+    from kavor.utils.context import reset_context, set_context
+
     nblk = 8
-    pools = [torch.zeros(nblk, 2, 256, hkv, 128, dtype=torch.bfloat16) for _ in range(shape["num_hidden_layers"])]
+    pools = [torch.zeros(nblk, 2, 256, hkv, 128, dtype=torch.bfloat16) for _ in model.model.layers]
     for lyr, pool in zip(model.model.layers, pools):
         lyr.self_attn.attn.k_cache = [pool[:, 0]]
         lyr.self_attn.attn.v_cache = [pool[:, 1]]
@@ -319,6 +340,8 @@ def main() -> int:
     torch.save(golden_layer(), out / "layer_golden.pt")
     torch.save(golden_tiny_model(), out / "tiny_model_golden.pt")
     torch.save(golden_tiny_model(decode_steps=31, keep_logits=False), out / "tiny_model_golden_32.pt")
+    for family in cases.FAMILIES:
+        torch.save(golden_family_model(family), out / f"{family}_tiny_golden.pt")
     (out / "host_trace.json").write_text(json.dumps(golden_host_trace()))
     dist.destroy_process_group()
     for f in sorted(out.glob("*golden*")) + [out / "host_trace.json"]:

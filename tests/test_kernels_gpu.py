@@ -109,8 +109,12 @@ def test_rope_matches_oracle(interleaved):
     close(dk, k_ref, 2e-2, 2e-2)
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 8), (32, 8), (4, 1), (64, 8)])
-def test_fused_qknorm_rope_store(hq, hkv):
+@pytest.mark.parametrize("hq,hkv,qk_norm,interleaved", [
+    (16, 8, True, False), (32, 8, True, False), (4, 1, True, False), (64, 8, True, False),
+    (32, 8, False, False),   # Mistral: no q/k norm
+    (16, 2, False, True),    # ERNIE 4.5: no q/k norm, interleaved pairs
+])
+def test_fused_qknorm_rope_store(hq, hkv, qk_norm, interleaved):
     from kavor_b200.layers.rotary_embedding import build_cos_sin_cache
 
     T, hd, bs, nblk = 19, 128, 256, 3
@@ -124,12 +128,13 @@ def test_fused_qknorm_rope_store(hq, hkv):
     q = qkv[:, :hq * hd].view(T, hq, hd)
     k = qkv[:, hq * hd:(hq + hkv) * hd].view(T, hkv, hd)
     v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
-    q_ref = ops.rope(ops.rmsnorm(q, qw, EPS), pos, cache)
-    k_ref = ops.rope(ops.rmsnorm(k, kw, EPS), pos, cache)
+    qn, kn = (ops.rmsnorm(q, qw, EPS), ops.rmsnorm(k, kw, EPS)) if qk_norm else (q, k)
+    q_ref = ops.rope(qn, pos, cache, interleaved)
+    k_ref = ops.rope(kn, pos, cache, interleaved)
     pool = torch.zeros(nblk, 2, bs, hkv, hd, dtype=torch.bfloat16, device=DEV)
     d = qkv.to(DEV)
-    K().qknorm_rope_store(d, hq, hkv, hd, qw.to(DEV), kw.to(DEV), EPS, pos.to(DEV), cache.to(DEV).contiguous(), False,
-                          pool[:, 0], pool[:, 1], slots.to(DEV))
+    K().qknorm_rope_store(d, hq, hkv, hd, qw.to(DEV) if qk_norm else None, kw.to(DEV) if qk_norm else None, EPS,
+                          pos.to(DEV), cache.to(DEV).contiguous(), interleaved, pool[:, 0], pool[:, 1], slots.to(DEV))
     dq = d[:, :hq * hd].view(T, hq, hd).cpu()
     dk = d[:, hq * hd:(hq + hkv) * hd].view(T, hkv, hd).cpu()
     close(dq, q_ref, 2e-2, 2e-2)

@@ -1,5 +1,6 @@
 """Pin the CPU oracle to the reference: every restated op is checked against
 fixtures produced by the reference's own code (tests/golden/make_golden.py)."""
+import pytest
 import torch
 
 import cases
@@ -143,6 +144,31 @@ def test_tiny_model_32_greedy_tokens_match_reference_model():
         batch = omodel.Batch(False, pos, slots, context_lens=ctx, block_tables=torch.tensor(tables, dtype=torch.int32))
         _, logits = omodel.forward(p, ids, batch, kv, shape)
     assert checked >= 84  # of 96 (3 sequences x 32 tokens)
+
+
+@pytest.mark.parametrize("family", cases.FAMILIES)
+def test_family_model_greedy_matches_reference_model(family):
+    """Tiny Mistral (no q/k norm, no bias) and ERNIE 4.5 (q/k/v bias,
+    interleaved RoPE, bf16 residual add before a plain RMSNorm): prefill + 8
+    decode steps of the reference model class, teacher-forced; logits cosine
+    >= 0.999 and the greedy token wherever the reference's top two logits are
+    more than two bf16 ulps apart."""
+    gold = _load(f"{family}_tiny_golden.pt")
+    shape = cases.family_oracle_shape(family)
+    p = cases.family_checkpoint(family, seed=5)
+    kv = [(torch.zeros(8, 256, shape.hkv, 128, dtype=torch.bfloat16),
+           torch.zeros(8, 256, shape.hkv, 128, dtype=torch.bfloat16)) for _ in range(shape.layers)]
+
+    def step(b):
+        if b["is_prefill"]:
+            batch = omodel.Batch(True, b["positions"], b["slot_mapping"], b["cu_seqlens"], b["cu_seqlens"])
+        else:
+            batch = omodel.Batch(False, b["positions"], b["slot_mapping"], context_lens=b["context_lens"],
+                                 block_tables=b["block_tables"])
+        return omodel.forward(p, b["input_ids"], batch, kv, shape, max_position=4096)[1]
+
+    checked = sum(cases.check_greedy_step(logits, rec) for logits, rec in cases.replay(gold, step))
+    assert checked >= 13  # at least half of the 27 tokens (the random-init logits are flat)
 
 
 def test_philox_known_answer():

@@ -17,13 +17,13 @@ def _port():
         return s.getsockname()[1]
 
 
-def _tiny_cfg():
+def _tiny_cfg(family="qwen3"):
     import cases
 
-    return cases.hf_config(cases.TINY)
+    return cases.hf_config(cases.TINY) if family == "qwen3" else cases.family_config(family)
 
 
-def _shard_worker(rank, port, out):
+def _shard_worker(rank, port, out, family):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -36,7 +36,7 @@ def _shard_worker(rank, port, out):
         from kavor_b200.models import AutoModelForCausalLM
 
         torch.set_default_dtype(torch.bfloat16)
-        cfg = _tiny_cfg()
+        cfg = _tiny_cfg(family)
         model = AutoModelForCausalLM.model_class(cfg)(cfg)
         AutoModelForCausalLM.load_weight(model, cfg, load_format="dummy", seed=4)
         pool = CachePool(model, SimpleNamespace(), WORLD)
@@ -46,7 +46,8 @@ def _shard_worker(rank, port, out):
         dist.destroy_process_group()
 
 
-def test_tp2_shards_reassemble_the_tp1_weights():
+@pytest.mark.parametrize("family", ["qwen3", "ernie4_5"])  # ernie4_5: q/k/v biases shard with their rows
+def test_tp2_shards_reassemble_the_tp1_weights(family):
     import torch.multiprocessing as mp
 
     from kavor_b200.models import AutoModelForCausalLM
@@ -55,7 +56,7 @@ def test_tp2_shards_reassemble_the_tp1_weights():
     with ctx.Manager() as m:
         out = m.dict()
         port = _port()
-        ps = [ctx.Process(target=_shard_worker, args=(r, port, out)) for r in range(WORLD)]
+        ps = [ctx.Process(target=_shard_worker, args=(r, port, out, family)) for r in range(WORLD)]
         for p in ps:
             p.start()
         for p in ps:
@@ -66,7 +67,7 @@ def test_tp2_shards_reassemble_the_tp1_weights():
     prev = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     try:
-        cfg = _tiny_cfg()
+        cfg = _tiny_cfg(family)
         full = AutoModelForCausalLM.model_class(cfg)(cfg)
         AutoModelForCausalLM.load_weight(full, cfg, load_format="dummy", seed=4)
     finally:

@@ -45,7 +45,9 @@ const char* kvb_last_error(void);
 
 /* OR of the device-side error bits raised by kernels on the CURRENT device
  * since the last clear (1: block table, 2: slot, 4: wait timeout, 8: token id,
- * 16: peer (all-reduce flag) wait timeout). Synchronises the device. Returns 0 or a CUDA error. */
+ * 16: peer (all-reduce flag) wait timeout, 32: a launch configuration the
+ * kernel cannot serve, its work skipped). Synchronises the device. Returns 0
+ * or a CUDA error. */
 int kvb_device_error(unsigned* bits, int clear);
 
 /* Number of SMs of the current device (used by the host-side heuristics). */
@@ -189,10 +191,12 @@ int kvb_gemm_workspace_size(int M, int N, int K, int splits, size_t* bytes);
  * in TMEM, bf16 result; rows of x, w, y with leading dimensions ldx, ldw, ldy
  * (elements; x and w rows 16-byte aligned). The weight is streamed once per
  * token tile (up to 256 tokens) through TMA. splits = 0 lets a cost model
- * pick the token tile and the K split; splits in {1, 2, 4, 8, 16} forces the
- * split (a thread-block cluster of that many CTAs whose fp32 parts are summed
- * in a fixed order through distributed shared memory: deterministic).
- * `workspace` is unused (may be NULL). */
+ * pick the token tile and the K split (among 1, 2, 4, 8, 16); splits in 1..16
+ * asks for that split (a thread-block cluster of that many CTAs whose fp32
+ * parts are summed in a fixed order through distributed shared memory:
+ * deterministic), falling back to the cost model's choice when no token tile
+ * can take it (more CTAs than K-steps, or a reduction that does not fit the
+ * CTA's shared memory). `workspace` is unused (may be NULL). */
 int kvb_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
                   int splits, void* workspace, size_t workspace_bytes, void* stream);
 
@@ -209,6 +213,12 @@ int kvb_gemm_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, v
  * width; gated = the fused SiLU form): plan[0] token tile, plan[1] K splits,
  * plan[2] work units, plan[3] CTAs. */
 int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan);
+
+/* Process-wide tuning of kvb_gemm_bf16 / kvb_gemm_silu_bf16 (no reference
+ * counterpart): the producer asks L2 for the weight K-steps `ksteps` ahead of
+ * its TMA loads (cp.async.bulk.prefetch.tensor; 0 = off, the default; at most
+ * 64). Applies to launches made after the call. */
+int kvb_gemm_set_l2_prefetch(int ksteps);
 
 /* ---------------------------------------- tensor-parallel all-reduce (NVLink) */
 

@@ -273,6 +273,12 @@ def gemm_plan(M: int, N: int, K: int, splits: int = 0, gated: bool = False) -> d
     return {"mt": out[0], "splits": out[1], "units": out[2], "grid": out[3]}
 
 
+def gemm_set_l2_prefetch(ksteps: int) -> None:
+    """Weight K-steps the GEMM producer prefetches into L2 ahead of its TMA
+    loads, for every later launch in this process (0 = off, the default)."""
+    _lib.call("kvb_gemm_set_l2_prefetch", int(ksteps))
+
+
 def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
     """y = x @ weight^T on tcgen05 tensor cores (bf16 in/out, fp32 accumulate)."""
     _cuda(x, "x", _BF16)

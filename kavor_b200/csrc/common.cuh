@@ -39,6 +39,7 @@ enum DeviceError : unsigned {
   kErrTimeout = 1u << 2,      // bounded mbarrier / flag wait gave up
   kErrTokenId = 1u << 3,      // embedding id outside the vocabulary
   kErrPeerTimeout = 1u << 4,  // cross-GPU flag wait gave up
+  kErrConfig = 1u << 5,       // a launch configuration the kernel cannot serve (work skipped)
 };
 
 // Host-side error message helpers (defined in capi.cu).

@@ -27,12 +27,18 @@
 //   cluster     (K split over C = 2..16 CTAs of one thread-block cluster, one
 //               unit per CTA): when its MMAs are done every CTA pushes its fp32
 //               accumulator through distributed shared memory into the CTAs
-//               that own each 128/C-feature slice (the stage ring, idle by
+//               that own each slice of the tile's sixteen 8-feature groups
+//               (16 / C groups each when C divides 16; the stage ring, idle by
 //               then, is the landing buffer), and each owner sums the C parts
 //               in cluster-rank order — deterministic — and writes bf16. No
 //               global scratch memory and no atomics.
+// Optionally (kvb_gemm_set_l2_prefetch) the producer also asks L2 for the
+// weight K-steps a fixed distance ahead of its TMA loads, so the loads that
+// fill the ring wait on L2 rather than HBM latency.
 // No cluster multicast is used anywhere (multi-GPU safe).
 #include <cudaTypedefs.h>
+
+#include <atomic>
 
 #include "common.cuh"
 #include "../../include/kavor_b200.h"
@@ -58,6 +64,8 @@ struct GemmArgs {
   int up_row0;      // gated: first weight row of the up half (= output width)
   uint32_t idesc;
   int vec_out;      // y rows are 16-byte aligned
+  int pf;           // weight K-steps to prefetch into L2 ahead of the TMA loads (0: none)
+  int gmax;         // cluster split: most 8-feature groups any rank owns (ceil(16 / splits))
 };
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
@@ -65,6 +73,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
+}
+
+// Ask for the box at (c0, c1) to be brought into L2 (no shared memory, no
+// barrier): the weight stream reaches the later TMA loads from L2 instead of HBM.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 // K-major operand tile [rows][64 bf16] with 128-byte swizzle: 8-row groups of
@@ -234,6 +250,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
       for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
         int n_tile, m_tile, split, kb0, nkb;
         unit_coords(a, u, n_tile, m_tile, split, kb0, nkb);
+        // weight K-steps [first, pf) go to L2 now, step i + pf after step i's
+        // load; the first S steps of the CTA's first unit are loaded at once
+        const int first = u == (int)blockIdx.x ? S : 0;
+        for (int j = first; j < a.pf && j < nkb; ++j) {
+          tma_prefetch_l2_2d(&wmap, (kb0 + j) * kBK, n_tile * kBN);
+          if constexpr (G) tma_prefetch_l2_2d(&wmap, (kb0 + j) * kBK, a.up_row0 + n_tile * kBN);
+        }
         for (int i = 0; i < nkb; ++i, ++it) {
           const int s = it % S;
           if (it >= S && !mbar_wait(smem_u32(&empty_bar[s]), ((it / S) - 1) & 1, &g_err_gemm)) {
@@ -246,6 +269,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
           tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n_tile * kBN, fb);
           if constexpr (G) tma_load_2d(sa + kABytes, &wmap, (kb0 + i) * kBK, a.up_row0 + n_tile * kBN, fb);
           tma_load_2d(sa + C::kA * kABytes, &xmap, (kb0 + i) * kBK, m_tile * MT, fb);
+          const int j = i + a.pf;
+          if (a.pf > 0 && j < nkb && j >= first) {
+            tma_prefetch_l2_2d(&wmap, (kb0 + j) * kBK, n_tile * kBN);
+            if constexpr (G) tma_prefetch_l2_2d(&wmap, (kb0 + j) * kBK, a.up_row0 + n_tile * kBN);
+          }
         }
       }
     }
@@ -345,22 +373,30 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     // ring is free; push the fp32 accumulator slices to their owners
     __syncwarp();
     cluster_sync_all();
+    // The tile's 16 groups of 8 features are dealt to the C ranks in order,
+    // rank o owning groups [16 o / C, 16 (o + 1) / C) (128 / C features each
+    // when C divides 16). The landing buffer holds, per slab and source rank,
+    // gmax groups of 8 rows of kPitch floats.
     const int Cn = a.splits;
-    const int fpc = kBN / Cn;  // features owned by each cluster rank
+    const int rows_per_src = a.gmax * 8;
     const uint32_t rank = cluster_rank();
+    const bool fits = C::kA * Cn * rows_per_src * C::kPitch * 4 <= S * C::kStageBytes;  // the host plan ensures it
+    if (!fits && threadIdx.x == 0) atomicOr(&g_err_gemm, (unsigned)kErrConfig);
     int n_tile, m_tile, split, kb0, nkb;
     unit_coords(a, blockIdx.x, n_tile, m_tile, split, kb0, nkb);
     const uint32_t red = smem_u32(smem);
-    if (warp >= kEpiWarp0 && !dead) {
+    if (warp >= kEpiWarp0 && !dead && fits) {
       constexpr int CH = C::kChunk;
       const int q = warp & 3;
       const int f = q * 32 + lane;
-      const uint32_t owner = (uint32_t)(f / fpc);
-      const int fl = f % fpc;
+      const int grp = f >> 3;
+      const int owner = ((grp + 1) * Cn + 15) / 16 - 1;
+      const int fl = (grp - owner * 16 / Cn) * 8 + (f & 7);  // row inside the owner's part
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int h = 0; h < C::kA; ++h) {
-        const uint32_t dst = map_to_rank(red + (uint32_t)((((h * Cn + (int)rank) * fpc + fl) * C::kPitch) * 4), owner);
+        const uint32_t dst =
+            map_to_rank(red + (uint32_t)((((h * Cn + (int)rank) * rows_per_src + fl) * C::kPitch) * 4), (uint32_t)owner);
 #pragma unroll 1
         for (int c = 0; c < MT; c += CH) {
           float v[32];
@@ -378,12 +414,13 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     tc_fence_before();
     __syncwarp();
     cluster_sync_all();
-    // part 3: this CTA owns features [rank * fpc, (rank + 1) * fpc) of the tile
-    if (warp >= kEpiWarp0 && !dead) {
+    // part 3: this CTA owns feature groups [g0, g0 + ng) of the tile
+    if (warp >= kEpiWarp0 && !dead && fits) {
       const float* rf = reinterpret_cast<const float*>(smem);
       const int e = threadIdx.x - kEpiWarp0 * 32;
-      const int groups = (fpc / 8) * MT;
-      const int n0 = n_tile * kBN + (int)rank * fpc, m0 = m_tile * MT;
+      const int g0 = (int)rank * 16 / Cn, ng = ((int)rank + 1) * 16 / Cn - g0;
+      const int groups = ng * MT;
+      const int n0 = n_tile * kBN + g0 * 8, m0 = m_tile * MT;
 #pragma unroll 1
       for (int g = e; g < groups; g += 128) {
         const int ml = g % MT, fg = g / MT;
@@ -394,11 +431,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
         for (int j = 0; j < 8; ++j) acc[j] = acu[j] = 0.f;
 #pragma unroll 1
         for (int s = 0; s < Cn; ++s) {
-          const float* p = rf + ((s * fpc + fg * 8) * C::kPitch + ml);
+          const float* p = rf + ((s * rows_per_src + fg * 8) * C::kPitch + ml);
 #pragma unroll
           for (int j = 0; j < 8; ++j) acc[j] += p[j * C::kPitch];
           if constexpr (G) {
-            const float* pu = p + Cn * fpc * C::kPitch;
+            const float* pu = p + Cn * rows_per_src * C::kPitch;
 #pragma unroll
             for (int j = 0; j < 8; ++j) acu[j] += pu[j * C::kPitch];
           }
@@ -456,6 +493,10 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
   return kOk;
 }
 
+// K-steps of weight the producer asks L2 for ahead of its TMA loads
+// (kvb_gemm_set_l2_prefetch; 0 = off).
+std::atomic<int> g_l2_prefetch{0};
+
 int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -485,6 +526,16 @@ constexpr TileShape kGatedShapes[] = {{16, Cfg<16, true, false>::kStages, Cfg<16
                                       {32, Cfg<32, true, false>::kStages, Cfg<32, true, false>::kPerSm},
                                       {64, Cfg<64, true, false>::kStages, Cfg<64, true, false>::kPerSm},
                                       {128, Cfg<128, true, false>::kStages, Cfg<128, true, false>::kPerSm}};
+
+// The cluster split's landing buffer (the stage ring) holds, per weight slab
+// and source rank, ceil(16 / C) groups of 8 feature rows of (mt + 4) floats.
+bool landing_fits(int mt, bool gated, int stages, int splits) {
+  if (splits <= 1) return true;
+  const int slabs = gated ? 2 : 1;
+  const int64_t rows = (int64_t)slabs * splits * ((16 + splits - 1) / splits) * 8;
+  const int64_t ring = (int64_t)stages * (slabs * kABytes + mt * kBK * 2);
+  return rows * (mt + 4) * 4 <= ring;
+}
 
 Plan finish_plan(int M, int N, int K, int mt, int per_sm, int splits) {
   Plan p;
@@ -534,7 +585,8 @@ double plan_cost(const Plan& p, int M, int N, int K, int per_sm, int slabs) {
 }
 
 // N is the OUTPUT width (for the gated form: the intermediate size I).
-// splits_req > 0 forces the K split (cluster size, at most 16).
+// splits_req > 0 forces the K split (cluster size 1..16; the automatic choice
+// considers powers of two).
 Plan make_plan(int M, int N, int K, int splits_req, bool gated = false) {
   Plan best{};
   double best_t = 1e30;
@@ -542,14 +594,18 @@ Plan make_plan(int M, int N, int K, int splits_req, bool gated = false) {
   const TileShape* shapes = gated ? kGatedShapes : kShapes;
   const int nshapes = gated ? 4 : 5;
   static const int kSplits[] = {1, 2, 4, 8, 16};
+  const int forced[] = {splits_req};
+  const int* cand = splits_req > 0 ? forced : kSplits;
+  const int ncand = splits_req > 0 ? 1 : 5;
   for (int si = 0; si < nshapes; ++si) {
     const TileShape& sh = shapes[si];
     if (sh.mt > 16 && sh.mt >= 2 * M) continue;  // a token tile far above the batch wastes tensor work
-    for (int s : kSplits) {
-      if (splits_req > 0 && s != splits_req) continue;
+    for (int ci = 0; ci < ncand; ++ci) {
+      const int s = cand[ci];
       Plan p = finish_plan(M, N, K, sh.mt, sh.per_sm, s);
       if (p.splits != s) continue;
       if (p.splits > 1 && (int64_t)(p.splits - 1) * p.kb_per_split >= p.kb_total) continue;  // an empty part
+      if (!landing_fits(sh.mt, gated, sh.stages, p.splits)) continue;
       const double t = plan_cost(p, M, N, K, sh.per_sm, slabs);
       if (t < best_t * 0.97) {
         best_t = t;
@@ -631,6 +687,8 @@ int run_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, in
   a.units = p.units;
   a.up_row0 = n_out;
   a.vec_out = ((uintptr_t)y & 15) == 0 && ldy % 8 == 0;
+  a.pf = g_l2_prefetch.load(std::memory_order_relaxed);
+  a.gmax = (16 + p.splits - 1) / p.splits;
   cudaStream_t st = (cudaStream_t)stream;
   if (gated) {
     switch (p.mt) {
@@ -679,6 +737,12 @@ extern "C" int kvb_gemm_silu_bf16(const void* x, int64_t ldx, const void* w, int
   (void)workspace;
   (void)workspace_bytes;
   return run_gemm(x, ldx, w, ldw, y, ldy, M, inter, K, splits, stream, true, "kvb_gemm_silu_bf16");
+}
+
+extern "C" int kvb_gemm_set_l2_prefetch(int ksteps) {
+  if (ksteps < 0 || ksteps > 64) return set_error(kInvalid, "kvb_gemm_set_l2_prefetch: ksteps must be in [0, 64]");
+  g_l2_prefetch.store(ksteps, std::memory_order_relaxed);
+  return kOk;
 }
 
 extern "C" int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan) {

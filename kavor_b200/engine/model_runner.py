@@ -426,7 +426,8 @@ class ModelRunner:
             return
         bits = _lib.device_error(clear=True)
         if bits:
-            names = {1: "block table", 2: "slot mapping", 4: "wait timeout", 8: "token id", 16: "peer wait timeout"}
+            names = {1: "block table", 2: "slot mapping", 4: "wait timeout", 8: "token id", 16: "peer wait timeout",
+                     32: "launch configuration"}
             what = ", ".join(n for b, n in names.items() if bits & b)
             raise RuntimeError(f"rank {self.rank}: device-side error bits {bits:#x} ({what}) within the last "
                                f"{self.DEVICE_CHECK_EVERY} steps")

@@ -2,7 +2,11 @@
 plan and every forced K split), kvb_gemm_silu_bf16 for the gate-up shapes, and
 cuBLAS (torch.matmul) on the same operands.
 
-    python -m kavor_b200.profile_gemm [M,M,...]      (default 1,64,256)
+    python -m kavor_b200.profile_gemm [M,M,...] [--splits 1,2,3,4,8,16] [--l2-prefetch 0,4]
+
+(default M 1,64,256; K splits 1,2,4,8,16; L2 prefetch distance 0). Every
+variant runs at every L2 prefetch distance given (kvb_gemm_set_l2_prefetch);
+labels carry a "_pfN" suffix when N > 0.
 
 Shapes: QKV, O, gate-up, down and LM head of Qwen3-8B at TP=1 and TP=8. Each
 timing is one replay of a CUDA graph of 20 launches (device time, CUDA events),
@@ -13,8 +17,8 @@ token tile, max |y - cuBLAS|] per variant, then prefill-size lines (M = 2048,
 """
 from __future__ import annotations
 
+import argparse
 import json
-import sys
 
 import torch
 
@@ -41,7 +45,13 @@ def _timeit(fn, iters=20):
 
 
 def main(argv=None) -> int:
-    argv = sys.argv[1:] if argv is None else argv
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("ms", nargs="?", default="1,64,256")
+    ap.add_argument("--splits", default="1,2,4,8,16")
+    ap.add_argument("--l2-prefetch", default="0")
+    a = ap.parse_args(argv)
+    split_list = [int(v) for v in a.splits.split(",")]
+    pf_list = [int(v) for v in a.l2_prefetch.split(",")]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     _lib.load()
@@ -50,7 +60,7 @@ def main(argv=None) -> int:
         for name, N, Kd in (("qkv", 6144 // tp, 4096), ("o", 4096, 4096 // tp), ("gate_up", 24576 // tp, 4096),
                             ("down", 4096, 12288 // tp), ("lm_head", 151936 // tp, 4096)):
             shapes.append((f"{name}_tp{tp}", N, Kd))
-    Ms = [int(x) for x in argv[0].split(",")] if argv else [1, 64, 256]
+    Ms = [int(x) for x in a.ms.split(",")]
     for M in Ms:
         for name, N, Kd in shapes:
             wbytes = N * Kd * 2
@@ -61,24 +71,30 @@ def main(argv=None) -> int:
             ref = torch.matmul(x, ws[0].t())
             res = {"M": M, "shape": name, "N": N, "K": Kd, "copies": len(ws), "plan": K.gemm_plan(M, N, Kd)}
             nbytes = wbytes + M * Kd * 2 + M * N * 2
-            for label, splits in (("auto", 0), ("s1", 1), ("s2", 2), ("s4", 4), ("s8", 8), ("s16", 16)):
-                p = K.gemm_plan(M, N, Kd, splits)
-                if splits and p["splits"] != splits:
-                    continue
-                K.gemm(x, ws[0], out=out, splits=splits)
-                err = (out.float() - ref.float()).abs().max().item()
-                t = _timeit(lambda i: K.gemm(x, ws[i % len(ws)], out=out, splits=splits))
-                res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"], round(err, 4)]
-            t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
-            res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
-            if name.startswith("gate_up"):
-                og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
-                for label, splits in (("g_auto", 0), ("g_s1", 1), ("g_s2", 2), ("g_s4", 4), ("g_s8", 8)):
-                    p = K.gemm_plan(M, N // 2, Kd, splits, True)
+            for pf in pf_list:
+                K.gemm_set_l2_prefetch(pf)
+                sfx = f"_pf{pf}" if pf else ""
+                for splits in [0] + split_list:
+                    label = ("auto" if splits == 0 else f"s{splits}") + sfx
+                    p = K.gemm_plan(M, N, Kd, splits)
                     if splits and p["splits"] != splits:
                         continue
-                    t = _timeit(lambda i: K.gemm_silu(x, ws[i % len(ws)], out=og, splits=splits))
-                    res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"]]
+                    K.gemm(x, ws[0], out=out, splits=splits)
+                    err = (out.float() - ref.float()).abs().max().item()
+                    t = _timeit(lambda i: K.gemm(x, ws[i % len(ws)], out=out, splits=splits))
+                    res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"], round(err, 4)]
+                if name.startswith("gate_up"):
+                    og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+                    for splits in [0] + [s for s in split_list if s <= 8]:
+                        label = ("g_auto" if splits == 0 else f"g_s{splits}") + sfx
+                        p = K.gemm_plan(M, N // 2, Kd, splits, True)
+                        if splits and p["splits"] != splits:
+                            continue
+                        t = _timeit(lambda i: K.gemm_silu(x, ws[i % len(ws)], out=og, splits=splits))
+                        res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"]]
+            K.gemm_set_l2_prefetch(0)
+            t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
+            res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
             res["device_error_bits"] = _lib.device_error(clear=True)
             print(json.dumps(res), flush=True)
             del ws

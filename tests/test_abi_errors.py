@@ -64,6 +64,8 @@ CASES = [
      INVALID, "bad arguments"),
     ("kvb_gemm_plan", (0, 64, 64, 0, 0, ctypes.cast(ctypes.create_string_buffer(16), ctypes.POINTER(ctypes.c_int))),
      INVALID, "bad sizes"),
+    ("kvb_gemm_set_l2_prefetch", (-1,), INVALID, "ksteps"),
+    ("kvb_gemm_set_l2_prefetch", (65,), INVALID, "ksteps"),
 ]
 
 
@@ -71,6 +73,11 @@ CASES = [
 def test_bad_arguments_are_rejected_on_the_host(lib, name, args, status, fragment):
     assert _status(lib, name, *args) == status
     assert fragment in _message(lib)
+
+
+def test_tuning_knob_accepts_its_range(lib):
+    assert lib.kvb_gemm_set_l2_prefetch(64) == 0
+    assert lib.kvb_gemm_set_l2_prefetch(0) == 0
 
 
 def test_empty_work_is_success(lib):

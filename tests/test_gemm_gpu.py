@@ -63,7 +63,7 @@ def test_gemm_back_to_back_splits_of_different_tile_counts():
     a previous call left behind."""
     from kavor_b200 import _kernels as K_
 
-    shapes = [(256, 6144, 4096, 3, False), (256, 24576, 4096, 2, False), (64, 1536, 4096, 4, True),
+    shapes = [(256, 6144, 4096, 0, False), (256, 24576, 4096, 2, False), (64, 1536, 4096, 4, True),
               (256, 12288, 4096, 2, True), (16, 151936 // 8, 4096, 16, False), (256, 24576, 4096, 1, False), (1, 768, 4096, 8, False)]
     for i, (M, N, K, splits, gated) in enumerate(shapes * 2):
         x, w = _inputs(M, (2 if gated else 1) * N, K, seed=10 + i)

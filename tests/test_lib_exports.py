@@ -93,6 +93,28 @@ def test_gemm_plans_are_consistent(lib):
             assert K.gemm_workspace_bytes(M, N, Kd) == 0  # the split reduces through distributed shared memory
 
 
+def test_gemm_forced_splits_of_any_cluster_size(lib):
+    """A requested K split of 1..16 CTAs is taken exactly when every part gets
+    K-steps (ceil(kb / C) per part, the last one non-empty); the reduction fits
+    the stage ring of some token tile at every such split for these shapes
+    (the 128-token tile and smaller take any C), otherwise the cost model's
+    own plan is used."""
+    import math
+
+    from kavor_b200 import _kernels as K
+
+    for splits in range(1, 17):
+        for M, N, Kd in ((256, 6144, 4096), (64, 4096, 12288), (1, 768, 4096), (100, 1000, 1536)):
+            p = K.gemm_plan(M, N, Kd, splits)
+            kb = math.ceil(Kd / 64)
+            if (splits - 1) * math.ceil(kb / splits) < kb:
+                assert p["splits"] == splits, (M, N, Kd, splits, p)
+                assert p["units"] == math.ceil(N / 128) * math.ceil(M / p["mt"]) * splits
+                assert splits == 1 or (p["grid"] == p["units"] and p["units"] % splits == 0)
+            else:
+                assert p == K.gemm_plan(M, N, Kd)
+
+
 def test_allreduce_plan_matches_the_documented_choice(lib):
     """Host-side mode choice of the fused all-reduce (no launch): peer one-shot
     at 2 ranks, switch one-shot below 8 rows per rank and switch two-shot from

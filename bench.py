@@ -57,6 +57,10 @@ def parse_args(argv=None):
     ap.add_argument("--context", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gemm", choices=["cublas", "tcgen05"], default="cublas",
+                    help="GEMM of the projections (Config.gemm_backend)")
+    ap.add_argument("--gemm-l2-prefetch", type=int, default=0,
+                    help="tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads")
     return ap.parse_args(argv)
 
 
@@ -71,8 +75,10 @@ def measured_peaks() -> tuple[float, str]:
 
 
 def model_shape(name: str) -> dict:
-    from kavor_b200.config import QWEN3_PRESETS
+    from kavor_b200.config import FAMILY_PRESETS, QWEN3_PRESETS
 
+    if name in FAMILY_PRESETS:
+        return dict(FAMILY_PRESETS[name])
     d = dict(QWEN3_PRESETS[name])
     d["vocab_size"] = 151936
     return d
@@ -179,8 +185,17 @@ class CpuDecodeSample:
         pos = torch.full((batch,), context - 1)
         slots = tables[:, (context - 1) // 256] * 256 + (context - 1) % 256
         self.batch = om.Batch(False, pos, slots, context_lens=ctx, block_tables=tables)
-        self.cache = ops.cos_sin_cache(hd, context + 1, 1e6)
-        self.shape = om.Shape(hidden=H, inter=I, layers=1, hq=hq, hkv=hkv)
+        family = shape.get("model_type", "qwen3")
+        ernie = family == "ernie4_5"
+        if family != "qwen3":  # Mistral / ERNIE 4.5: no q/k norm; ERNIE: optional q/k/v bias
+            del self.p[pre + "self_attn.q_norm.weight"], self.p[pre + "self_attn.k_norm.weight"]
+        bias = ernie and bool(shape.get("use_bias", False))
+        if bias:
+            for n, rows in (("q", hq), ("k", hkv), ("v", hkv)):
+                self.p[pre + f"self_attn.{n}_proj.bias"] = fill(rows * hd)
+        self.cache = ops.cos_sin_cache(hd, context + 1, float(shape.get("rope_theta", 1e6)))
+        self.shape = om.Shape(hidden=H, inter=I, layers=1, hq=hq, hkv=hkv, qk_norm=family == "qwen3",
+                              qkv_bias=bias, interleaved=ernie, separate_residual_add=ernie)
         self.h = fill(batch, H) * 100
         self.layer()  # warm-up
         head_w = fill(shape["vocab_size"], H)
@@ -230,7 +245,7 @@ def run_reference(args) -> int:
 def _config(args) -> dict:
     return {"workload": f"{args.model} decode step, batch {args.batch}, context {args.context}, TP={args.gpus}",
             "model": args.model, "global_batch": args.batch, "context": args.context, "block_size": 256,
-            "parallelism": f"tp{args.gpus}",
+            "parallelism": f"tp{args.gpus}", "gemm": args.gemm, "gemm_l2_prefetch": args.gemm_l2_prefetch,
             "l2": "inputs larger than L2 (per step: all weights + every sequence's KV pages)"}
 
 
@@ -295,7 +310,8 @@ def run_ours(args) -> int:
     model_dir = write_model_dir(os.path.join(tmp, f"r{rank}"), args.model)
     cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world, max_model_len=max_len,
                  max_num_seqs=B, max_num_batched_tokens=4096, num_kvcache_blocks=B * blocks_per_seq + 8,
-                 rdzv_port=1, graph_batch_sizes=(B,))
+                 rdzv_port=1, graph_batch_sizes=(B,), gemm_backend=args.gemm,
+                 gemm_l2_prefetch=args.gemm_l2_prefetch)
     runner = ModelRunner(cfg, rank, None)
     with torch.no_grad():
         runner.cache.pools.view(torch.bfloat16).normal_(0.0, 1.0)  # resident KV pages, N(0, 1)

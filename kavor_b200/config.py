@@ -3,8 +3,10 @@
 Extra fields over the reference: ``load_format`` ("auto" reads the checkpoint
 in ``model``, "dummy" draws a seeded random checkpoint of the same shapes),
 ``seed`` for that draw, ``enable_prefix_caching`` (the reference always
-caches prefixes) and ``graph_batch_sizes`` (the decode batch buckets captured
-as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16).
+caches prefixes), ``graph_batch_sizes`` (the decode batch buckets captured
+as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16),
+``fused_allreduce``, and ``gemm_backend`` / ``gemm_l2_prefetch`` (which GEMM
+the projections use, and its L2 prefetch distance).
 """
 from __future__ import annotations
 
@@ -51,6 +53,8 @@ class Config:
     enable_prefix_caching: bool = True
     graph_batch_sizes: tuple[int, ...] | None = None  # decode buckets to capture (None: 1,2,4,8,16,32,...)
     fused_allreduce: bool = True  # TP > 1: NVLink all-reduce fused with add+RMSNorm (False: NCCL + separate norm)
+    gemm_backend: str = "cublas"  # projections: "cublas" (F.linear) or "tcgen05" (kvb_gemm_bf16, fused gate-up+SiLU)
+    gemm_l2_prefetch: int = 0     # tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads (0 = off)
 
     def __post_init__(self):
         if not os.path.isdir(self.model):
@@ -58,6 +62,8 @@ class Config:
         assert self.kvcache_block_size % 256 == 0, "kvcache_block_size must be a multiple of 256"
         assert 1 <= self.tensor_parallel_size <= 8
         assert self.load_format in ("auto", "dummy")
+        assert self.gemm_backend in ("cublas", "tcgen05"), "gemm_backend must be 'cublas' or 'tcgen05'"
+        assert 0 <= self.gemm_l2_prefetch <= 64
         self.rdzv_port = self.rdzv_port if self.rdzv_port > 0 else free_port()
         if self.hf_config is None:
             self.hf_config = load_hf_config(self.model)

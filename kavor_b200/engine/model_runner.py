@@ -31,6 +31,7 @@ from kavor_b200 import _lib
 from kavor_b200.engine.cache_pool import CachePool
 from kavor_b200.engine.sequence import Sequence
 from kavor_b200.layers.allreduce import TPAllReduce, set_tp_allreduce
+from kavor_b200.layers.linear import set_gemm_backend
 from kavor_b200.layers.sampler import Sampler
 from kavor_b200.models import AutoModelForCausalLM
 from kavor_b200.utils.context import reset_context, set_context
@@ -198,6 +199,9 @@ class ModelRunner:
             raise RuntimeError(f"process group has {dist.get_world_size()} ranks, config asks for {self.world_size}")
         self.device = torch.device("cuda", self._local_device(rank))
         torch.cuda.set_device(self.device)
+        set_gemm_backend(config.gemm_backend)
+        if config.gemm_backend == "tcgen05":
+            K.gemm_set_l2_prefetch(config.gemm_l2_prefetch)
         prev_dtype = torch.get_default_dtype()
         torch.set_default_dtype(torch.bfloat16)
         torch.set_default_device(self.device)

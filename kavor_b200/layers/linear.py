@@ -5,7 +5,10 @@ split the output rows across ranks (QKV rows ordered [q | k | v] per rank,
 gate/up rows [gate | up] per rank), row-parallel layers split the input
 columns and all-reduce the partial products (bias added on rank 0 only).
 All projections go through ``linear()``, the single GEMM entry point of the
-package.
+package. Which GEMM runs is a process-wide choice (``set_gemm_backend``):
+"cublas" (torch's F.linear, the reference's own GEMM; the default) or
+"tcgen05" (this package's kernel, kvb_gemm_bf16, with the gate-up projection
+and SiluAndMul fused into kvb_gemm_silu_bf16 by the MLP).
 """
 from __future__ import annotations
 
@@ -21,9 +24,31 @@ def divide(numerator: int, denominator: int) -> int:
     return numerator // denominator
 
 
+GEMM_BACKENDS = ("cublas", "tcgen05")
+_GEMM_BACKEND = "cublas"
+
+
+def set_gemm_backend(name: str) -> None:
+    global _GEMM_BACKEND
+    if name not in GEMM_BACKENDS:
+        raise ValueError(f"unknown GEMM backend {name!r} (one of {GEMM_BACKENDS})")
+    _GEMM_BACKEND = name
+
+
+def gemm_backend() -> str:
+    return _GEMM_BACKEND
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x W^T (+ b) in bf16 with fp32 accumulation (cuBLAS through torch)."""
+    """y = x W^T (+ b) in bf16 with fp32 accumulation."""
+    if _GEMM_BACKEND == "tcgen05":
+        from kavor_b200 import _kernels as K
+
+        y = K.gemm(x, weight, out=out)
+        if bias is not None:
+            y.add_(bias)
+        return y
     if out is None:
         return F.linear(x, weight, bias)
     torch.matmul(x, weight.t(), out=out)

@@ -22,7 +22,8 @@ from kavor_b200.layers.allreduce import get_tp_allreduce
 from kavor_b200.layers.attention import Attention
 from kavor_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
 from kavor_b200.layers.layernorm import RMSNorm
-from kavor_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp
+from kavor_b200.layers.linear import (MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp,
+                                      gemm_backend)
 from kavor_b200.layers.rotary_embedding import get_rope
 from kavor_b200.utils.context import get_context
 
@@ -104,6 +105,8 @@ class Qwen3MLP(nn.Module):
         self.act_fn = SiluAndMul()
 
     def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+        if gemm_backend() == "tcgen05":  # gate-up projection and SiluAndMul in one kernel
+            return self.down_proj(K.gemm_silu(x, self.gate_up_proj.weight), reduce=reduce, out=out)
         return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce, out=out)
 
 

@@ -78,8 +78,25 @@ def _model(cfg):
 CASES = [("qwen3", "tiny_model_golden.pt")] + [(f, f"{f}_tiny_golden.pt") for f in cases.FAMILIES]
 
 
+@pytest.fixture(params=["cublas", "tcgen05"])
+def gemm_backend(request, monkeypatch):
+    """Both GEMM backends of linear(): torch's F.linear, or the package's
+    kernel entry points (replaced here by the oracle's linear, with the gate-up
+    + SiLU fusion of the MLP as silu_mul(linear))."""
+    from kavor_b200 import _kernels as K
+    from kavor_b200.layers import linear as L
+
+    if request.param == "tcgen05":
+        monkeypatch.setattr(K, "gemm", lambda x, w, out=None, splits=0: ops.linear(x, w) if out is None
+                            else out.copy_(ops.linear(x, w)))
+        monkeypatch.setattr(K, "gemm_silu", lambda x, w, out=None, splits=0: ops.silu_mul(ops.linear(x, w)))
+    L.set_gemm_backend(request.param)
+    yield request.param
+    L.set_gemm_backend("cublas")
+
+
 @pytest.mark.parametrize("family,fixture", CASES, ids=[c[0] for c in CASES])
-def test_model_classes_replay_reference_greedy(oracle_kernels, family, fixture):
+def test_model_classes_replay_reference_greedy(oracle_kernels, gemm_backend, family, fixture):
     from kavor_b200.utils.context import reset_context, set_context
 
     cfg = cases.hf_config(cases.TINY) if family == "qwen3" else cases.family_config(family)
@@ -108,6 +125,14 @@ def test_model_classes_replay_reference_greedy(oracle_kernels, family, fixture):
     # than the GPU's 0.999: a wrong rope theta or rotation stays above 0.998
     checked = sum(cases.check_greedy_step(logits, rec, min_cos=0.9999) for logits, rec in cases.replay(gold, step))
     assert checked >= 13  # at least half of the 27 tokens
+
+
+def test_gemm_backend_names():
+    from kavor_b200.layers import linear as L
+
+    with pytest.raises(ValueError, match="unknown GEMM backend"):
+        L.set_gemm_backend("triton")
+    assert L.gemm_backend() == "cublas"
 
 
 def test_family_attention_flags():

@@ -61,6 +61,8 @@ def parse_args(argv=None):
                     help="GEMM of the projections (Config.gemm_backend)")
     ap.add_argument("--gemm-l2-prefetch", type=int, default=0,
                     help="tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads")
+    ap.add_argument("--e2e-pipelined", action="store_true",
+                    help="e2e through ModelRunner.run_async with one step in flight (host work overlaps the GPU)")
     return ap.parse_args(argv)
 
 
@@ -414,29 +416,25 @@ def run_ours(args) -> int:
     # --- end to end through ModelRunner.run (sequences advance one token per step)
     e2e = None
     if not args.no_e2e:
-        def e2e_step():
-            for s in seqs:
-                bm.may_append_block(s)
-            toks = runner.run(seqs, False)
-            for s, t in zip(seqs, toks):
-                s.num_cached_tokens += 1
-                s.append_token(t)
+        from kavor_b200.engine.model_runner import advance_decode
 
-        for _ in range(args.warmup):
-            e2e_step()
+        def run_e2e(n):
+            advance_decode(runner, seqs, bm, n, pipelined=args.e2e_pipelined)
+
+        run_e2e(args.warmup)
         barrier()
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        run_e2e(args.steps)
         f1.record()
         torch.cuda.synchronize()
         barrier()
         t_e2e = max_over_ranks(f0.elapsed_time(f1) / 1e3)
         e2e = {"value": B * args.steps / t_e2e, "unit": "tok/s", "ms_per_step": t_e2e / args.steps * 1e3,
                "h2d_bytes_per_step": runner.decode_buffers.nbytes, "d2h_bytes_per_step": 8 * B,
-               "api": "ModelRunner.run(seqs, is_prefill=False)"}
+               "api": ("ModelRunner.run_async(seqs, chain=True), one step in flight" if args.e2e_pipelined
+                       else "ModelRunner.run(seqs, is_prefill=False)")}
 
     dev_err = _lib.device_error(clear=True)
     cpu = None

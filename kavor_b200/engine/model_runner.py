@@ -20,6 +20,7 @@ import datetime
 import itertools
 import os
 import pickle
+import time
 from multiprocessing.shared_memory import SharedMemory
 
 import numpy as np
@@ -37,6 +38,7 @@ from kavor_b200.models import AutoModelForCausalLM
 from kavor_b200.utils.context import reset_context, set_context
 
 SHM_BYTES = 1 << 22
+MAILBOX_WAIT_S = 60.0  # rank 0 waits at most this long for every worker to take the previous message
 
 
 # ----------------------------------------------------------------- host metadata
@@ -134,11 +136,16 @@ class Staging:
 
 
 class DecodeBuffers:
-    """Static device inputs of the decode graphs (fixed addresses) with a pinned
-    host mirror; one copy per step moves all of them."""
+    """Static device inputs of the decode graphs (fixed addresses) with pinned
+    host mirrors; one copy per step moves all of them. Mirror 0 serves the
+    synchronous ``ModelRunner.run``; mirrors 1 and 2 alternate between the
+    steps of ``run_async``, so a mirror is never rewritten while the copy of
+    the step before is still queued. Sampled tokens come back through two
+    alternating pinned buffers."""
 
     FIELDS = (("input_ids", np.int64), ("positions", np.int64), ("temperatures", np.float32),
               ("slot_mapping", np.int32), ("context_lens", np.int32))
+    MIRRORS = 3
 
     def __init__(self, max_bs: int, max_blocks: int, device: torch.device):
         self.max_bs, self.max_blocks = max_bs, max_blocks
@@ -149,19 +156,26 @@ class DecodeBuffers:
         layout["block_tables"] = (off, np.int32, (max_bs, max_blocks))
         off += max_bs * max_blocks * 4
         self.nbytes = off
-        self.host = torch.zeros(off, dtype=torch.uint8, device="cpu", pin_memory=True)
+        self.hosts = [torch.zeros(off, dtype=torch.uint8, device="cpu", pin_memory=True) for _ in range(self.MIRRORS)]
+        self.host = self.hosts[0]
         self.dev = torch.zeros(off, dtype=torch.uint8, device=device)
-        self.h, self.d = {}, {}
-        hv = self.host.numpy()
+        self.views: list[dict] = [{} for _ in range(self.MIRRORS)]
+        self.d = {}
         for name, (o, dt, shape) in layout.items():
             n = int(np.prod(shape)) * np.dtype(dt).itemsize
-            self.h[name] = hv[o:o + n].view(dt).reshape(shape)
+            for m in range(self.MIRRORS):
+                self.views[m][name] = self.hosts[m].numpy()[o:o + n].view(dt).reshape(shape)
             self.d[name] = self.dev[o:o + n].view(torch.from_numpy(np.zeros(0, dt)).dtype).view(shape)
+        self.h = self.views[0]
+        self.copied: list[torch.cuda.Event | None] = [None] * self.MIRRORS
         self.sampled = torch.zeros(max_bs, dtype=torch.int64, device=device)
+        self.tokens_host = [torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True) for _ in range(2)]
 
-    def fill(self, meta: dict, temperatures: np.ndarray, bucket: int) -> None:
+    def fill(self, meta: dict, temperatures: np.ndarray, bucket: int, mirror: int = 0) -> None:
+        if self.copied[mirror] is not None:  # the previous copy out of this mirror has been read
+            self.copied[mirror].synchronize()
         n = meta["input_ids"].shape[0]
-        h = self.h
+        h = self.views[mirror]
         h["input_ids"][:n] = meta["input_ids"]
         h["input_ids"][n:bucket] = 0
         h["positions"][:n] = meta["positions"]
@@ -175,7 +189,57 @@ class DecodeBuffers:
         bt = meta["block_tables"]
         h["block_tables"][:n, :bt.shape[1]] = bt
         h["block_tables"][:n, bt.shape[1]:] = -1
-        self.dev.copy_(self.host, non_blocking=True)
+        self.dev.copy_(self.hosts[mirror], non_blocking=True)
+        if mirror:
+            self.copied[mirror] = torch.cuda.Event()
+            self.copied[mirror].record()
+
+
+class PendingDecode:
+    """A decode step issued by ``ModelRunner.run_async``: ``result()`` waits for
+    the step and returns its sampled token ids (read from pinned memory)."""
+
+    def __init__(self, host: torch.Tensor, event: torch.cuda.Event, n: int):
+        self.host, self.event, self.n = host, event, n
+        self.done = False
+
+    def result(self) -> list[int]:
+        self.event.synchronize()
+        self.done = True
+        return self.host[:self.n].tolist()
+
+
+def advance_decode(runner, seqs: list[Sequence], block_manager, steps: int, pipelined: bool = False) -> None:
+    """Run `steps` decode steps of a fixed batch, growing every sequence by one
+    token per step (blocks from `block_manager`). Synchronous: ``runner.run``
+    per step. Pipelined: ``runner.run_async`` with one step in flight — step
+    i+1 is issued, its input tokens chained on the device, before step i's
+    tokens are read back; the host appends a placeholder (-1) per step and
+    patches it when the tokens arrive, so the sequences end the same either
+    way while the host's per-step work overlaps the GPU's."""
+    if not pipelined:
+        for _ in range(steps):
+            for s in seqs:
+                block_manager.may_append_block(s)
+            for s, t in zip(seqs, runner.run(seqs, False)):
+                s.num_cached_tokens += 1
+                s.append_token(t)
+        return
+    pending = None
+    for _ in range(steps):
+        for s in seqs:
+            block_manager.may_append_block(s)
+        nxt = runner.run_async(seqs, chain=pending is not None)
+        if pending is not None:
+            for s, t in zip(seqs, pending.result()):
+                s.token_ids[-1] = s.last_token = t
+        for s in seqs:
+            s.num_cached_tokens += 1
+            s.append_token(-1)
+        pending = nxt
+    if pending is not None:
+        for s, t in zip(seqs, pending.result()):
+            s.token_ids[-1] = s.last_token = t
 
 
 # ----------------------------------------------------------------- runner
@@ -189,6 +253,8 @@ class ModelRunner:
         self.rank = rank
         self.event = event
         self.shm = None
+        self._async_steps, self._async_bs = 0, 0
+        self._pending: list[PendingDecode | None] = [None, None]
         self.owns_process_group = False
         if not dist.is_initialized():
             dist.init_process_group("nccl", f"tcp://127.0.0.1:{config.rdzv_port}", world_size=self.world_size,
@@ -271,6 +337,15 @@ class ModelRunner:
         data = pickle.dumps([method, *args])
         if len(data) + 4 > len(self.shm.buf):
             raise RuntimeError(f"TP message of {len(data)} bytes exceeds the {len(self.shm.buf)}-byte mailbox")
+        # every worker has taken the previous message (a worker clears its event
+        # after reading): calls that return before the step completes
+        # (run_async) can otherwise come back before a worker has read
+        deadline = time.monotonic() + MAILBOX_WAIT_S
+        for ev in self.event:
+            while ev.is_set():
+                if time.monotonic() > deadline:
+                    raise RuntimeError(f"a TP worker did not take the previous message within {MAILBOX_WAIT_S:.0f} s")
+                time.sleep(0)
         self.shm.buf[0:4] = len(data).to_bytes(4, "little")
         self.shm.buf[4:len(data) + 4] = data
         for ev in self.event:
@@ -457,6 +532,13 @@ class ModelRunner:
             finally:
                 reset_context()
             return tokens.tolist()
+        bs = self._decode_launch(seqs, temps, mirror=0, chain=False)
+        return self.decode_buffers.sampled[:bs].tolist()
+
+    def _decode_launch(self, seqs: list[Sequence], temps: np.ndarray, mirror: int, chain: bool) -> int:
+        """Upload one decode step's metadata (through pinned mirror `mirror`),
+        optionally take the input tokens from the previous step's samples on
+        the device, and launch the step (graph replay, or eager)."""
         meta = decode_metadata(seqs, self.block_size)
         bs = len(seqs)
         self._ensure_decode_buffers()
@@ -465,7 +547,9 @@ class ModelRunner:
             raise RuntimeError(f"decode batch {bs} x {meta['block_tables'].shape[1]} blocks exceeds the "
                                f"runner's {buf.max_bs} x {buf.max_blocks}")
         bucket = next((b for b in getattr(self, "graph_bs", []) if b >= bs), bs)
-        buf.fill(meta, temps, bucket)
+        buf.fill(meta, temps, bucket, mirror)
+        if chain:
+            buf.d["input_ids"][:bs].copy_(buf.sampled[:bs])
         graph = self.graphs.get(bucket)
         if graph is not None:
             graph.replay()
@@ -477,4 +561,38 @@ class ModelRunner:
                 self._decode_forward(bs)
             finally:
                 reset_context()
-        return buf.sampled[:bs].tolist()
+        return bs
+
+    @torch.inference_mode()
+    def run_async(self, seqs: list[Sequence], chain: bool = False) -> PendingDecode | None:
+        """One decode step, issued without waiting for it (no reference
+        counterpart; ``run`` is the reference's synchronous call). With
+        ``chain``, every sequence's input token is the token the previous
+        ``run_async`` step sampled for it, copied on the device: the same
+        sequences in the same order, each grown on the host since by one
+        placeholder token (its value is not read). Returns a PendingDecode,
+        whose ``result()`` must be read before the step after the next one is
+        issued — except on a TP worker driven through the mailbox by rank 0,
+        which returns None (every rank samples the same tokens; rank 0 reads
+        them)."""
+        self._check_device()
+        k = self._async_steps % 2
+        self._async_steps += 1
+        mailbox_worker = self.rank > 0 and self.shm is not None
+        prev = self._pending[k]
+        if prev is not None and not prev.done and not mailbox_worker:
+            raise RuntimeError("run_async: the result of the step issued two calls ago has not been read")
+        if chain and len(seqs) != self._async_bs:
+            raise RuntimeError(f"run_async: a chained step needs the previous step's {self._async_bs} sequences")
+        temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
+        bs = self._decode_launch(seqs, temps, mirror=1 + k, chain=chain)
+        self._async_bs = bs
+        if mailbox_worker:
+            return None
+        buf = self.decode_buffers
+        host = buf.tokens_host[k]
+        host[:bs].copy_(buf.sampled[:bs], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._pending[k] = PendingDecode(host, ev, bs)
+        return self._pending[k]

@@ -248,3 +248,52 @@ def test_runner_forwards_run_under_inference_mode():
     from kavor_b200.engine.model_runner import ModelRunner
     for name in ("_profile_prefill", "_profile_decode", "capture_cudagraph", "run"):
         assert hasattr(getattr(ModelRunner, name), "__wrapped__"), name
+
+
+class _FakePending:
+    def __init__(self, tokens):
+        self.tokens = tokens
+
+    def result(self):
+        return list(self.tokens)
+
+
+class _FakeRunner:
+    """Host model of ModelRunner.run / run_async: the 'device' samples
+    (31 x input token + position) mod 1000; a chained step takes its input
+    tokens from the previous step's samples, never from the host."""
+
+    def __init__(self):
+        self.device_sampled = None
+
+    @staticmethod
+    def _sample(inputs, positions):
+        return [(31 * t + p) % 1000 for t, p in zip(inputs, positions)]
+
+    def run(self, seqs, is_prefill):
+        return self._sample([s.last_token for s in seqs], [len(s) - 1 for s in seqs])
+
+    def run_async(self, seqs, chain=False):
+        inputs = self.device_sampled if chain else [s.last_token for s in seqs]
+        assert all(t >= 0 for t in inputs), "a placeholder reached the model"
+        self.device_sampled = self._sample(inputs, [len(s) - 1 for s in seqs])
+        return _FakePending(self.device_sampled)
+
+
+@pytest.mark.parametrize("steps", [1, 2, 7])
+def test_pipelined_decode_ends_like_the_synchronous_one(make_seq, steps):
+    """advance_decode with one step in flight (placeholders patched on read,
+    inputs chained on the device) leaves every sequence, block table and
+    cached-token count exactly as the step-by-step loop does."""
+    from kavor_b200.engine.model_runner import advance_decode
+
+    runs = []
+    for pipelined in (False, True):
+        bm = BlockManager(64, BS)
+        seqs = [make_seq(range(10 + i, 13 + 2 * i)) for i in range(3)]
+        for s in seqs:
+            bm.allocate_prefill(s, 0)
+            s.num_cached_tokens = len(s)
+        advance_decode(_FakeRunner(), seqs, bm, steps, pipelined=pipelined)
+        runs.append([(s.token_ids, s.last_token, s.block_table, s.num_cached_tokens, len(s)) for s in seqs])
+    assert runs[0] == runs[1]

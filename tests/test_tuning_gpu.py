@@ -1,7 +1,9 @@
-"""GEMM tuning options that are off by default, against the same references as
-test_gemm_gpu.py: K splits whose cluster size is not a power of two (the
-reduction deals the tile's sixteen 8-feature groups unevenly over the ranks)
-and the L2 prefetch of the weight stream (kvb_gemm_set_l2_prefetch)."""
+"""Options that are off by default, against the same references as the
+default paths' tests: GEMM K splits whose cluster size is not a power of two
+(the reduction deals the tile's sixteen 8-feature groups unevenly over the
+ranks), the L2 prefetch of the weight stream (kvb_gemm_set_l2_prefetch), the
+tcgen05 GEMM backend inside the model, and pipelined decode
+(ModelRunner.run_async with one step in flight)."""
 import pytest
 import torch
 
@@ -73,3 +75,80 @@ def test_gemm_l2_prefetch_leaves_results_unchanged(ksteps):
         ref = fn(x, w, splits=splits)
         K_.gemm_set_l2_prefetch(ksteps)
         assert torch.equal(fn(x, w, splits=splits), ref), (M, N, K, splits, gated)
+
+
+@pytest.fixture(scope="module")
+def tiny_dir(tmp_path_factory):
+    from kavor_b200.config import write_model_dir
+
+    return write_model_dir(str(tmp_path_factory.mktemp("tiny")), "Qwen3-0.6B", num_hidden_layers=2,
+                           vocab_size=4096, max_position_embeddings=4096)
+
+
+def _runner(tiny_dir, **kw):
+    import torch.distributed as dist
+
+    from kavor_b200.config import Config
+    from kavor_b200.engine.model_runner import ModelRunner
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", "tcp://127.0.0.1:29565", world_size=1, rank=0,
+                                device_id=torch.device("cuda", 0))
+    cfg = Config(tiny_dir, load_format="dummy", seed=3, max_model_len=2048, max_num_seqs=16,
+                 max_num_batched_tokens=2048, num_kvcache_blocks=64, **kw)
+    return ModelRunner(cfg, 0, None)
+
+
+def _greedy_decode(runner, pipelined, steps=9):
+    from kavor_b200.engine.block_manager import BlockManager
+    from kavor_b200.engine.model_runner import advance_decode
+    from kavor_b200.engine.sequence import Sequence
+    from kavor_b200.sampling_params import SamplingParams
+
+    Sequence.block_size = 256
+    prompts = [[(5 * i + 11 * j) % 4000 + 1 for j in range(n)] for i, n in enumerate((300, 17, 255, 1))]
+    seqs = [Sequence(p, SamplingParams(max_tokens=64)) for p in prompts]
+    bm = BlockManager(runner.config.num_kvcache_blocks, 256)
+    for s in seqs:
+        s.temperature = 0.0
+        bm.allocate_prefill(s, 0)
+        s.num_scheduled_tokens = s.num_tokens
+    for s, t in zip(seqs, runner.run(seqs, True)):
+        s.num_cached_tokens, s.num_scheduled_tokens = s.num_tokens, 0
+        s.append_token(t)
+        s.is_prefill = False
+    advance_decode(runner, seqs, bm, steps, pipelined=pipelined)
+    return [s.token_ids for s in seqs]
+
+
+def test_pipelined_decode_gives_the_synchronous_tokens(tiny_dir):
+    """Greedy decode through run_async (inputs chained on the device, one step
+    in flight) produces exactly the tokens of the synchronous run(); the 255-
+    token prompt crosses a block boundary during the steps."""
+    runner = _runner(tiny_dir)
+    try:
+        sync = _greedy_decode(runner, False)
+        piped = _greedy_decode(runner, True)
+    finally:
+        runner.exit()
+    assert piped == sync
+
+
+def test_tcgen05_gemm_backend_in_the_model(tiny_dir):
+    """The model with every projection on kvb_gemm_bf16 (gate-up + SiLU fused)
+    decodes greedily like the cuBLAS model (logits differ by summation order
+    only, so the tokens may part at a near-tie: compare the first steps)."""
+    from kavor_b200.layers.linear import set_gemm_backend
+
+    runs = []
+    for backend, pf in (("cublas", 0), ("tcgen05", 0), ("tcgen05", 8)):
+        runner = _runner(tiny_dir, gemm_backend=backend, gemm_l2_prefetch=pf)
+        try:
+            runs.append(_greedy_decode(runner, False, steps=3))
+        finally:
+            runner.exit()
+            set_gemm_backend("cublas")
+    assert runs[1] == runs[2]  # the prefetch changes no bit
+    prompt_lens = (300, 17, 255, 1)
+    same = sum(a[:n + 2] == b[:n + 2] for a, b, n in zip(runs[0], runs[1], prompt_lens))
+    assert same >= 3  # prefill token and first decode token of at least 3 of the 4 sequences

@@ -50,6 +50,15 @@ const char* kvb_last_error(void);
  * or a CUDA error. */
 int kvb_device_error(unsigned* bits, int clear);
 
+/* Launch mode of every later kernel launch from this process on the CURRENT
+ * device (no reference counterpart): 1 = programmatic dependent launch (each
+ * kernel may be scheduled while the kernel before it on the stream still
+ * runs; it waits at its start, griddepcontrol.wait, until that kernel has
+ * completed, so results are unchanged), 0 = plain stream-ordered launches
+ * (the default). Synchronous (it writes a device constant); call it outside
+ * stream capture. */
+int kvb_set_pdl(int enable);
+
 /* Number of SMs of the current device (used by the host-side heuristics). */
 int kvb_sm_count(int* out);
 

@@ -273,6 +273,13 @@ def gemm_plan(M: int, N: int, K: int, splits: int = 0, gated: bool = False) -> d
     return {"mt": out[0], "splits": out[1], "units": out[2], "grid": out[3]}
 
 
+def set_pdl(enable: bool) -> None:
+    """Programmatic dependent launch for every later kernel launch of this
+    process (each kernel is scheduled while the one before it on the stream
+    still runs and waits at its start for it; results are unchanged)."""
+    _lib.call("kvb_set_pdl", 1 if enable else 0)
+
+
 def gemm_set_l2_prefetch(ksteps: int) -> None:
     """Weight K-steps the GEMM producer prefetches into L2 ahead of its TMA
     loads, for every later launch in this process (0 = off, the default)."""

@@ -5,8 +5,9 @@ in ``model``, "dummy" draws a seeded random checkpoint of the same shapes),
 ``seed`` for that draw, ``enable_prefix_caching`` (the reference always
 caches prefixes), ``graph_batch_sizes`` (the decode batch buckets captured
 as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16),
-``fused_allreduce``, and ``gemm_backend`` / ``gemm_l2_prefetch`` (which GEMM
-the projections use, and its L2 prefetch distance).
+``fused_allreduce``, ``gemm_backend`` / ``gemm_l2_prefetch`` (which GEMM
+the projections use, and its L2 prefetch distance) and ``pdl`` (programmatic
+dependent launch of the package's kernels).
 """
 from __future__ import annotations
 
@@ -55,6 +56,7 @@ class Config:
     fused_allreduce: bool = True  # TP > 1: NVLink all-reduce fused with add+RMSNorm (False: NCCL + separate norm)
     gemm_backend: str = "cublas"  # projections: "cublas" (F.linear) or "tcgen05" (kvb_gemm_bf16, fused gate-up+SiLU)
     gemm_l2_prefetch: int = 0     # tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads (0 = off)
+    pdl: bool = False             # programmatic dependent launch of the package's kernels (kvb_set_pdl)
 
     def __post_init__(self):
         if not os.path.isdir(self.model):

@@ -327,6 +327,7 @@ __device__ void copy_rows(const ArArgs& a, int t, const bf16* src) {
 // resident at once, so no block can wait on a peer block that is not running.
 template <int W, int NCH>
 __global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __grid_constant__ ArArgs a) {
+  kernel_entry();
   __shared__ float red[kThreads / 32];
   __shared__ uint32_t v_s;
   __shared__ int ok_s;
@@ -393,11 +394,10 @@ __global__ void __launch_bounds__(kThreads, 2) ar_add_rmsnorm_kernel(const __gri
 template <int W>
 cudaError_t launch_w(const ArArgs& a, int blocks, int nch, cudaStream_t st) {
   const int per = (nch + kThreads - 1) / kThreads;
-  if (per <= 1) ar_add_rmsnorm_kernel<W, 1><<<blocks, kThreads, 0, st>>>(a);
-  else if (per <= 2) ar_add_rmsnorm_kernel<W, 2><<<blocks, kThreads, 0, st>>>(a);
-  else if (per <= 4) ar_add_rmsnorm_kernel<W, 4><<<blocks, kThreads, 0, st>>>(a);
-  else ar_add_rmsnorm_kernel<W, 8><<<blocks, kThreads, 0, st>>>(a);
-  return cudaGetLastError();
+  if (per <= 1) return launch_kernel(ar_add_rmsnorm_kernel<W, 1>, dim3(blocks), dim3(kThreads), 0, st, a);
+  if (per <= 2) return launch_kernel(ar_add_rmsnorm_kernel<W, 2>, dim3(blocks), dim3(kThreads), 0, st, a);
+  if (per <= 4) return launch_kernel(ar_add_rmsnorm_kernel<W, 4>, dim3(blocks), dim3(kThreads), 0, st, a);
+  return launch_kernel(ar_add_rmsnorm_kernel<W, 8>, dim3(blocks), dim3(kThreads), 0, st, a);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -1,6 +1,9 @@
-// Library-level entry points: version, error reporting, device queries.
+// Library-level entry points: version, error reporting, device queries,
+// launch mode.
 #include <stdarg.h>
 #include <stdio.h>
+
+#include <atomic>
 
 #include "common.cuh"
 #include "../../include/kavor_b200.h"
@@ -17,6 +20,10 @@ int set_error(int status, const char* fmt, ...) {
   return status;
 }
 
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
 int cuda_status(cudaError_t e, const char* where) {
   if (e == cudaSuccess) return kOk;
   set_error((int)e, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
@@ -30,6 +37,12 @@ int read_device_error_prefill(unsigned*, int);
 int read_device_error_sampler(unsigned*, int);
 int read_device_error_gemm(unsigned*, int);
 int read_device_error_allreduce(unsigned*, int);
+int set_pdl_trigger_elementwise(int);
+int set_pdl_trigger_decode(int);
+int set_pdl_trigger_prefill(int);
+int set_pdl_trigger_sampler(int);
+int set_pdl_trigger_gemm(int);
+int set_pdl_trigger_allreduce(int);
 
 }  // namespace kvb
 
@@ -51,6 +64,19 @@ extern "C" int kvb_device_error(unsigned* bits, int clear) {
     acc |= w;
   }
   *bits = acc;
+  return kvb::kOk;
+}
+
+extern "C" int kvb_set_pdl(int enable) {
+  if (enable != 0 && enable != 1) return kvb::set_error(kvb::kInvalid, "kvb_set_pdl: enable must be 0 or 1");
+  int (*setters[])(int) = {kvb::set_pdl_trigger_elementwise, kvb::set_pdl_trigger_decode,
+                           kvb::set_pdl_trigger_prefill, kvb::set_pdl_trigger_sampler, kvb::set_pdl_trigger_gemm,
+                           kvb::set_pdl_trigger_allreduce};
+  for (auto fn : setters) {
+    int rc = fn(enable);
+    if (rc) return rc;
+  }
+  kvb::g_pdl.store(enable, std::memory_order_relaxed);
   return kvb::kOk;
 }
 

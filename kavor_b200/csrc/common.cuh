@@ -173,10 +173,52 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// ---------------------------------------------------- programmatic dependent launch
+// Every kernel starts with kernel_entry(): wait until the grids it depends on
+// have completed and their writes are visible (griddepcontrol.wait; returns at
+// once when the kernel was launched without a programmatic dependency). With
+// programmatic launch on (kvb_set_pdl), it then lets the next kernel of the
+// stream be scheduled early (it stops at its own wait), so that kernel's launch
+// and CTA dispatch overlap this kernel's run; off (the default), the next
+// kernel starts after this one ends, as with plain launches. Nothing touches
+// global memory before the wait. The switch is a per-translation-unit
+// constant, written by kvb_set_pdl through set_pdl_trigger_<tag>().
+static __constant__ int c_pdl_trigger = 0;
+
+__device__ __forceinline__ void kernel_entry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (c_pdl_trigger) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launches made with programmatic stream serialization (kvb_set_pdl) or as
+// plain stream-ordered launches (the default).
+bool pdl_enabled();
+
+template <typename... Params, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  if (!pdl_enabled()) {
+    kernel<<<grid, block, smem, stream>>>(static_cast<Args&&>(args)...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 }  // namespace kvb
 
 // Every translation unit that launches kernels defines its own error word and
-// a host reader; capi.cu ORs them together for kvb_device_error().
+// a host reader; capi.cu ORs them together for kvb_device_error(). It also
+// defines the setter of its programmatic-launch switch (kvb_set_pdl).
 #define KVB_DEFINE_ERROR_WORD(tag)                                                  \
   namespace kvb {                                                                   \
   __device__ unsigned g_err_##tag = 0;                                              \
@@ -189,5 +231,9 @@ __device__ __forceinline__ float warp_sum(float v) {
       if (e != cudaSuccess) return cuda_status(e, "clear device error word");       \
     }                                                                               \
     return 0;                                                                       \
+  }                                                                                 \
+  int set_pdl_trigger_##tag(int on) {                                               \
+    cudaError_t e = cudaMemcpyToSymbol(c_pdl_trigger, &on, sizeof(int));            \
+    return e == cudaSuccess ? 0 : cuda_status(e, "set launch mode");                \
   }                                                                                 \
   }

@@ -64,6 +64,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
 __global__ void __launch_bounds__(kThreads, 2)
     decode_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                        const __grid_constant__ DecodeArgs a) {
+  kernel_entry();
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kStages];
   __shared__ __align__(8) uint64_t empty_bar[kStages];
@@ -272,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // Merge num_splits partial results per (sequence, query head).
 __global__ void decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     bf16* __restrict__ out, int64_t o_st, int64_t o_sh, int hq, int splits) {
+  kernel_entry();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int64_t base = ((int64_t)b * hq + h) * splits;
   float M = -INFINITY;
@@ -438,13 +440,13 @@ extern "C" int kvb_paged_decode_attn(const void* q, int64_t q_stride_t, int64_t 
   a.scale_log2 = scale * 1.4426950408889634f;
 
   dim3 grid(splits, num_kv_heads, batch);
-  decode_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(kmap, vmap, a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e =
+      launch_kernel(decode_attn_kernel, grid, dim3(kThreads), kSmemBytes, (cudaStream_t)stream, kmap, vmap, a);
   if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn launch");
   if (splits > 1) {
-    decode_merge_kernel<<<dim3(num_q_heads, batch), kHD, 0, (cudaStream_t)stream>>>(
-        a.part_o, a.part_lse, (bf16*)out, out_stride_t, out_stride_h, num_q_heads, splits);
-    e = cudaGetLastError();
+    e = launch_kernel(decode_merge_kernel, dim3(num_q_heads, batch), dim3(kHD), 0, (cudaStream_t)stream,
+                      (const float*)a.part_o, (const float*)a.part_lse, (bf16*)out, out_stride_t, out_stride_h,
+                      num_q_heads, splits);
     if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn merge launch");
   }
   return kOk;
@@ -560,13 +562,13 @@ extern "C" int kvb_paged_decode_attn_no_alloc(const void* q, int64_t q_stride_t,
   a.scale_log2 = scale * 1.4426950408889634f;
 
   dim3 grid(splits, num_kv_heads, batch);
-  decode_attn_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(kmap, vmap, a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e =
+      launch_kernel(decode_attn_kernel, grid, dim3(kThreads), kSmemBytes, (cudaStream_t)stream, kmap, vmap, a);
   if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc launch");
   if (splits > 1) {
-    decode_merge_kernel<<<dim3(num_q_heads, batch), kHD, 0, (cudaStream_t)stream>>>(
-        a.part_o, a.part_lse, (bf16*)out, out_stride_t, out_stride_h, num_q_heads, splits);
-    e = cudaGetLastError();
+    e = launch_kernel(decode_merge_kernel, dim3(num_q_heads, batch), dim3(kHD), 0, (cudaStream_t)stream,
+                      (const float*)a.part_o, (const float*)a.part_lse, (bf16*)out, out_stride_t, out_stride_h,
+                      num_q_heads, splits);
     if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc merge launch");
   }
   return kOk;

@@ -40,6 +40,7 @@ __global__ void store_kv_kernel(const bf16* __restrict__ key, int64_t key_stride
                                 int64_t value_stride, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
                                 int64_t num_slots, int64_t block_stride, int block_size, int row_elems,
                                 const int32_t* __restrict__ slot_mapping, int num_tokens) {
+  kernel_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= num_tokens) return;
@@ -66,6 +67,7 @@ __global__ void store_kv_kernel(const bf16* __restrict__ key, int64_t key_stride
 __global__ void rmsnorm128_kernel(const bf16* __restrict__ x, int64_t xst, int64_t xsh, bf16* __restrict__ out,
                                   int64_t ost, int64_t osh, const bf16* __restrict__ w, int tokens, int heads,
                                   float eps) {
+  kernel_entry();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= tokens * heads) return;
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_row_kernel(const bf16* __
                                                                   int64_t xsh, bf16* __restrict__ out, int64_t ost,
                                                                   int64_t osh, const bf16* __restrict__ w,
                                                                   int heads, int n_cols, float eps) {
+  kernel_entry();
   __shared__ float red[kRowThreads / 32];
   const int t = blockIdx.x / heads, h = blockIdx.x - (blockIdx.x / heads) * heads;
   const Vec8* xr = reinterpret_cast<const Vec8*>(x + (int64_t)t * xst + (int64_t)h * xsh);
@@ -143,6 +146,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_row_kernel(const bf16* __
 __global__ void __launch_bounds__(kRowThreads) add_rmsnorm_kernel(const bf16* __restrict__ x, bf16* residual,
                                                                   bf16* out, const bf16* __restrict__ w, int n_cols,
                                                                   float eps) {
+  kernel_entry();
   __shared__ float red[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const Vec8* xr = reinterpret_cast<const Vec8*>(x + row * n_cols);
@@ -194,6 +198,7 @@ __global__ void rope_kernel(bf16* q, int64_t qst, int64_t qsh, bf16* k, int64_t 
                             const int64_t* __restrict__ positions, const float* __restrict__ cs,
                             int64_t max_position, int tokens, int q_heads, int k_heads, int head_dim,
                             int interleaved) {
+  kernel_entry();
   const int heads = q_heads + k_heads;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -222,6 +227,7 @@ __global__ void qknorm_rope_store_kernel(bf16* qkv, int64_t qkv_stride, int toke
                                          const float* __restrict__ cs, int64_t max_position, int interleaved,
                                          bf16* k_cache, bf16* v_cache, int64_t num_slots, int64_t block_stride,
                                          int block_size, const int32_t* __restrict__ slot_mapping) {
+  kernel_entry();
   const int heads = hq + 2 * hkv;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -287,6 +293,7 @@ __global__ void qknorm_rope_store_kernel(bf16* qkv, int64_t qkv_stride, int toke
 // ------------------------------------------------------------------ SiLU*mul
 __global__ void silu_mul_kernel(const bf16* __restrict__ x, int64_t xst, bf16* __restrict__ out, int64_t ost,
                                 int tokens, int inter) {
+  kernel_entry();
   const int nch = inter / 8;
   const int64_t total = (int64_t)tokens * nch;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -305,6 +312,7 @@ __global__ void silu_mul_kernel(const bf16* __restrict__ x, int64_t xst, bf16* _
 // ------------------------------------------------------------------ embedding
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ w, bf16* __restrict__ out,
                                  int hidden, int64_t vocab_start, int64_t vocab_end, int64_t vocab_size) {
+  kernel_entry();
   const int t = blockIdx.x;
   const int64_t id = ids[t];
   if (vocab_size > 0 && (id < 0 || id >= vocab_size) && threadIdx.x == 0)
@@ -342,10 +350,11 @@ extern "C" int kvb_store_kv(const void* key, int64_t key_stride, const void* val
     return set_error(kInvalid, "kvb_store_kv: rows and strides must be 16-byte aligned");
   if (block_stride < (int64_t)block_size * row)
     return set_error(kInvalid, "kvb_store_kv: block_stride smaller than one block");
-  store_kv_kernel<<<blocks_for(num_tokens, 8), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)key, key_stride, (const bf16*)value, value_stride, (bf16*)k_cache, (bf16*)v_cache,
-      num_blocks * block_size, block_stride, block_size, row, slot_mapping, num_tokens);
-  return cuda_status(cudaGetLastError(), "kvb_store_kv launch");
+  return cuda_status(launch_kernel(store_kv_kernel, dim3(blocks_for(num_tokens, 8)), dim3(256), 0, (cudaStream_t)stream,
+                                   (const bf16*)key, key_stride, (const bf16*)value, value_stride, (bf16*)k_cache,
+                                   (bf16*)v_cache, num_blocks * block_size, block_stride, block_size, row, slot_mapping,
+                                   num_tokens),
+                     "kvb_store_kv launch");
 }
 
 extern "C" int kvb_rmsnorm(const void* x, int64_t x_stride_t, int64_t x_stride_h, void* out, int64_t out_stride_t,
@@ -358,19 +367,19 @@ extern "C" int kvb_rmsnorm(const void* x, int64_t x_stride_t, int64_t x_stride_h
   if (rows > INT32_MAX) return set_error(kUnsupported, "kvb_rmsnorm: too many rows");
   if (n_cols == 128 && x_stride_t % 4 == 0 && x_stride_h % 4 == 0 && out_stride_t % 4 == 0 &&
       out_stride_h % 4 == 0 && ((uintptr_t)x & 7) == 0 && ((uintptr_t)out & 7) == 0 && ((uintptr_t)weight & 7) == 0) {
-    rmsnorm128_kernel<<<blocks_for(rows, 8), 256, 0, (cudaStream_t)stream>>>(
-        (const bf16*)x, x_stride_t, x_stride_h, (bf16*)out, out_stride_t, out_stride_h, (const bf16*)weight, tokens,
-        heads, eps);
-    return cuda_status(cudaGetLastError(), "kvb_rmsnorm launch");
+    return cuda_status(launch_kernel(rmsnorm128_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, (cudaStream_t)stream,
+                                     (const bf16*)x, x_stride_t, x_stride_h, (bf16*)out, out_stride_t, out_stride_h,
+                                     (const bf16*)weight, tokens, heads, eps),
+                       "kvb_rmsnorm launch");
   }
   if (n_cols % 8 || x_stride_t % 8 || x_stride_h % 8 || out_stride_t % 8 || out_stride_h % 8 || !aligned16(x) ||
       !aligned16(out) || !aligned16(weight))
     return set_error(kInvalid, "kvb_rmsnorm: rows must be 16-byte aligned (n_cols and strides multiples of 8)");
   if (n_cols > kRowThreads * kRowMaxChunks * 8) return set_error(kUnsupported, "kvb_rmsnorm: n_cols > 16384");
-  rmsnorm_row_kernel<<<(unsigned)rows, kRowThreads, 0, (cudaStream_t)stream>>>(
-      (const bf16*)x, x_stride_t, x_stride_h, (bf16*)out, out_stride_t, out_stride_h, (const bf16*)weight, heads,
-      n_cols, eps);
-  return cuda_status(cudaGetLastError(), "kvb_rmsnorm launch");
+  return cuda_status(launch_kernel(rmsnorm_row_kernel, dim3((unsigned)rows), dim3(kRowThreads), 0, (cudaStream_t)stream,
+                                   (const bf16*)x, x_stride_t, x_stride_h, (bf16*)out, out_stride_t, out_stride_h,
+                                   (const bf16*)weight, heads, n_cols, eps),
+                     "kvb_rmsnorm launch");
 }
 
 extern "C" int kvb_add_rmsnorm(const void* x, void* residual, void* out, const void* weight, int tokens, int n_cols,
@@ -381,9 +390,10 @@ extern "C" int kvb_add_rmsnorm(const void* x, void* residual, void* out, const v
   if (n_cols % 8 || !aligned16(x) || !aligned16(residual) || !aligned16(out) || !aligned16(weight))
     return set_error(kInvalid, "kvb_add_rmsnorm: rows must be 16-byte aligned");
   if (n_cols > kRowThreads * kRowMaxChunks * 8) return set_error(kUnsupported, "kvb_add_rmsnorm: n_cols > 16384");
-  add_rmsnorm_kernel<<<(unsigned)tokens, kRowThreads, 0, (cudaStream_t)stream>>>(
-      (const bf16*)x, (bf16*)residual, (bf16*)out, (const bf16*)weight, n_cols, eps);
-  return cuda_status(cudaGetLastError(), "kvb_add_rmsnorm launch");
+  return cuda_status(launch_kernel(add_rmsnorm_kernel, dim3((unsigned)tokens), dim3(kRowThreads), 0,
+                                   (cudaStream_t)stream, (const bf16*)x, (bf16*)residual, (bf16*)out,
+                                   (const bf16*)weight, n_cols, eps),
+                     "kvb_add_rmsnorm launch");
 }
 
 extern "C" int kvb_rope(void* q, int64_t q_stride_t, int64_t q_stride_h, void* k, int64_t k_stride_t,
@@ -394,10 +404,10 @@ extern "C" int kvb_rope(void* q, int64_t q_stride_t, int64_t q_stride_h, void* k
   if (tokens == 0 || q_heads + k_heads == 0) return kOk;
   if (!positions || !cos_sin || (q_heads && !q) || (k_heads && !k)) return set_error(kInvalid, "kvb_rope: NULL pointer");
   const int64_t rows = (int64_t)tokens * (q_heads + k_heads);
-  rope_kernel<<<blocks_for(rows, 8), 256, 0, (cudaStream_t)stream>>>(
-      (bf16*)q, q_stride_t, q_stride_h, (bf16*)k, k_stride_t, k_stride_h, positions, cos_sin, max_position, tokens,
-      q_heads, k_heads, head_dim, interleaved);
-  return cuda_status(cudaGetLastError(), "kvb_rope launch");
+  return cuda_status(launch_kernel(rope_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, (cudaStream_t)stream, (bf16*)q,
+                                   q_stride_t, q_stride_h, (bf16*)k, k_stride_t, k_stride_h, positions, cos_sin,
+                                   max_position, tokens, q_heads, k_heads, head_dim, interleaved),
+                     "kvb_rope launch");
 }
 
 extern "C" int kvb_qknorm_rope_store(void* qkv, int64_t qkv_stride, int tokens, int num_q_heads, int num_kv_heads,
@@ -421,11 +431,12 @@ extern "C" int kvb_qknorm_rope_store(void* qkv, int64_t qkv_stride, int tokens, 
       return set_error(kInvalid, "kvb_qknorm_rope_store: bad cache arguments");
   }
   const int64_t rows = (int64_t)tokens * (num_q_heads + 2 * num_kv_heads);
-  qknorm_rope_store_kernel<<<blocks_for(rows, 8), 256, 0, (cudaStream_t)stream>>>(
-      (bf16*)qkv, qkv_stride, tokens, num_q_heads, num_kv_heads, (const bf16*)q_weight, (const bf16*)k_weight, eps,
-      apply_norm, positions, cos_sin, max_position, interleaved, (bf16*)k_cache, (bf16*)v_cache,
-      num_blocks * (int64_t)block_size, block_stride, block_size, slot_mapping);
-  return cuda_status(cudaGetLastError(), "kvb_qknorm_rope_store launch");
+  return cuda_status(launch_kernel(qknorm_rope_store_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0,
+                                   (cudaStream_t)stream, (bf16*)qkv, qkv_stride, tokens, num_q_heads, num_kv_heads,
+                                   (const bf16*)q_weight, (const bf16*)k_weight, eps, apply_norm, positions, cos_sin,
+                                   max_position, interleaved, (bf16*)k_cache, (bf16*)v_cache,
+                                   num_blocks * (int64_t)block_size, block_stride, block_size, slot_mapping),
+                     "kvb_qknorm_rope_store launch");
 }
 
 extern "C" int kvb_silu_mul(const void* x, int64_t x_stride, void* out, int64_t out_stride, int tokens, int inter,
@@ -438,9 +449,9 @@ extern "C" int kvb_silu_mul(const void* x, int64_t x_stride, void* out, int64_t 
   const int64_t total = (int64_t)tokens * (inter / 8);
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  silu_mul_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>((const bf16*)x, x_stride, (bf16*)out, out_stride,
-                                                                     tokens, inter);
-  return cuda_status(cudaGetLastError(), "kvb_silu_mul launch");
+  return cuda_status(launch_kernel(silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0, (cudaStream_t)stream,
+                                   (const bf16*)x, x_stride, (bf16*)out, out_stride, tokens, inter),
+                     "kvb_silu_mul launch");
 }
 
 extern "C" int kvb_embedding(const int64_t* ids, const void* weight, void* out, int tokens, int hidden,
@@ -450,7 +461,7 @@ extern "C" int kvb_embedding(const int64_t* ids, const void* weight, void* out, 
   if (!ids || !weight || !out) return set_error(kInvalid, "kvb_embedding: NULL pointer");
   if (hidden % 8 || !aligned16(weight) || !aligned16(out))
     return set_error(kInvalid, "kvb_embedding: rows must be 16-byte aligned");
-  embedding_kernel<<<(unsigned)tokens, 128, 0, (cudaStream_t)stream>>>(ids, (const bf16*)weight, (bf16*)out, hidden,
-                                                                      vocab_start, vocab_end, vocab_size);
-  return cuda_status(cudaGetLastError(), "kvb_embedding launch");
+  return cuda_status(launch_kernel(embedding_kernel, dim3((unsigned)tokens), dim3(128), 0, (cudaStream_t)stream, ids,
+                                   (const bf16*)weight, (bf16*)out, hidden, vocab_start, vocab_end, vocab_size),
+                     "kvb_embedding launch");
 }

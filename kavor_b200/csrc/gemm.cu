@@ -206,6 +206,7 @@ template <int MT, bool G, bool CL>
 __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ GemmArgs a) {
+  kernel_entry();
   using C = Cfg<MT, G, CL>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -634,21 +635,24 @@ int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, GemmArgs& a, int gr
   }
   a.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MT >> 3) << 17) | ((uint32_t)(kBN >> 4) << 24);
   if constexpr (!CL) {
-    gemm_kernel<MT, G, CL><<<grid, kThreads, C::kSmem, stream>>>(wmap, xmap, a);
-    return cuda_status(cudaGetLastError(), "kvb_gemm launch");
+    return cuda_status(launch_kernel(gemm_kernel<MT, G, CL>, dim3(grid), dim3(kThreads), C::kSmem, stream, wmap, xmap,
+                                     a),
+                       "kvb_gemm launch");
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = a.splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cuda_status(cudaLaunchKernelEx(&cfg, gemm_kernel<MT, G, CL>, wmap, xmap, a), "kvb_gemm cluster launch");
   }
 }

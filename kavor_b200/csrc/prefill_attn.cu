@@ -104,6 +104,7 @@ __device__ __forceinline__ void load_kv_tile(const PrefillArgs& a, int b, int kv
 
 template <bool kPaged>
 __global__ void __launch_bounds__(kThreads, 2) prefill_attn_kernel(const __grid_constant__ PrefillArgs a) {
+  kernel_entry();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int qtile = gridDim.x - 1 - blockIdx.x;
@@ -348,6 +349,7 @@ template <bool kPaged>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ TcArgs a) {
+  kernel_entry();
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, kfull[2], vfull[2], kv_empty[2], s_full[2], s_empty[2], p_full[2],
       pv_full[2], pv_empty[2];
@@ -660,8 +662,8 @@ int launch_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& v
     if (e != cudaSuccess) return cuda_status(e, "prefill tc smem attribute");
     if (dev < 64) done |= 1ull << dev;
   }
-  prefill_tc_kernel<kPaged><<<grid, kTcThreads, kTcSmem, st>>>(qm, km, vm, a);
-  return cuda_status(cudaGetLastError(), "kvb_prefill_attn (tcgen05) launch");
+  return cuda_status(launch_kernel(prefill_tc_kernel<kPaged>, grid, dim3(kTcThreads), kTcSmem, st, qm, km, vm, a),
+                     "kvb_prefill_attn (tcgen05) launch");
 }
 
 template <bool kPaged>
@@ -771,9 +773,8 @@ extern "C" int kvb_prefill_attn(const void* q, int64_t q_stride_t, int64_t q_str
   dim3 grid((max_seqlen_q + kRows - 1) / kRows, num_q_heads, batch);
   int rc = paged ? ensure_attr<true>() : ensure_attr<false>();
   if (rc) return rc;
-  if (paged)
-    prefill_attn_kernel<true><<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(a);
-  else
-    prefill_attn_kernel<false><<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(a);
-  return cuda_status(cudaGetLastError(), "kvb_prefill_attn launch");
+  const cudaError_t e =
+      paged ? launch_kernel(prefill_attn_kernel<true>, grid, dim3(kThreads), kSmemBytes, (cudaStream_t)stream, a)
+            : launch_kernel(prefill_attn_kernel<false>, grid, dim3(kThreads), kSmemBytes, (cudaStream_t)stream, a);
+  return cuda_status(e, "kvb_prefill_attn launch");
 }

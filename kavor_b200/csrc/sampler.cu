@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const bf16* __restrict
                                                           const float* __restrict__ temps,
                                                           const int32_t* __restrict__ seed, int64_t* __restrict__ out,
                                                           int vocab, bool vec) {
+  kernel_entry();
   const int b = blockIdx.x;
   Best best = score_segment(logits + (int64_t)b * row_stride, vocab, 0, (int64_t)b * vocab, temps[b],
                             (uint32_t)seed[0], vec);
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(kThreads) sample_partial_kernel(const bf16* __
                                                                   float* __restrict__ best_val,
                                                                   int64_t* __restrict__ best_idx, int shard_vocab,
                                                                   int64_t vocab_offset, int64_t vocab_total, bool vec) {
+  kernel_entry();
   const int b = blockIdx.x;
   Best best = score_segment(logits + (int64_t)b * row_stride, shard_vocab, vocab_offset, (int64_t)b * vocab_total,
                             temps[b], (uint32_t)seed[0], vec);
@@ -176,6 +178,7 @@ __global__ void __launch_bounds__(kThreads) sample_partial_kernel(const bf16* __
 
 __global__ void sample_combine_kernel(const float* __restrict__ vals, const int64_t* __restrict__ idxs, int world,
                                       int64_t* __restrict__ out, int batch) {
+  kernel_entry();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   Best best = {-INFINITY, INT64_MAX};
@@ -197,9 +200,9 @@ extern "C" int kvb_sample(const void* logits, int64_t row_stride, const float* t
   if (batch == 0) return kOk;
   if (!logits || !temperatures || !seed || !out) return set_error(kInvalid, "kvb_sample: NULL pointer");
   const bool vec = ((uintptr_t)logits & 15) == 0 && row_stride % 8 == 0;
-  sample_kernel<<<batch, kThreads, 0, (cudaStream_t)stream>>>((const bf16*)logits, row_stride, temperatures, seed, out,
-                                                              vocab, vec);
-  return cuda_status(cudaGetLastError(), "kvb_sample launch");
+  return cuda_status(launch_kernel(sample_kernel, dim3(batch), dim3(kThreads), 0, (cudaStream_t)stream,
+                                   (const bf16*)logits, row_stride, temperatures, seed, out, vocab, vec),
+                     "kvb_sample launch");
 }
 
 extern "C" int kvb_sample_partial(const void* logits, int64_t row_stride, const float* temperatures,
@@ -212,10 +215,10 @@ extern "C" int kvb_sample_partial(const void* logits, int64_t row_stride, const 
   if (!logits || !temperatures || !seed || !best_val || !best_idx)
     return set_error(kInvalid, "kvb_sample_partial: NULL pointer");
   const bool vec = ((uintptr_t)logits & 15) == 0 && row_stride % 8 == 0;
-  sample_partial_kernel<<<batch, kThreads, 0, (cudaStream_t)stream>>>((const bf16*)logits, row_stride, temperatures,
-                                                                      seed, best_val, best_idx, shard_vocab,
-                                                                      vocab_offset, vocab_total, vec);
-  return cuda_status(cudaGetLastError(), "kvb_sample_partial launch");
+  return cuda_status(launch_kernel(sample_partial_kernel, dim3(batch), dim3(kThreads), 0, (cudaStream_t)stream,
+                                   (const bf16*)logits, row_stride, temperatures, seed, best_val, best_idx, shard_vocab,
+                                   vocab_offset, vocab_total, vec),
+                     "kvb_sample_partial launch");
 }
 
 extern "C" int kvb_sample_combine(const float* vals, const int64_t* idxs, int world_size, int64_t* out, int batch,
@@ -223,6 +226,7 @@ extern "C" int kvb_sample_combine(const float* vals, const int64_t* idxs, int wo
   if (batch < 0 || world_size <= 0) return set_error(kInvalid, "kvb_sample_combine: bad sizes");
   if (batch == 0) return kOk;
   if (!vals || !idxs || !out) return set_error(kInvalid, "kvb_sample_combine: NULL pointer");
-  sample_combine_kernel<<<(batch + 127) / 128, 128, 0, (cudaStream_t)stream>>>(vals, idxs, world_size, out, batch);
-  return cuda_status(cudaGetLastError(), "kvb_sample_combine launch");
+  return cuda_status(launch_kernel(sample_combine_kernel, dim3((batch + 127) / 128), dim3(128), 0, (cudaStream_t)stream,
+                                   vals, idxs, world_size, out, batch),
+                     "kvb_sample_combine launch");
 }

@@ -268,6 +268,8 @@ class ModelRunner:
         set_gemm_backend(config.gemm_backend)
         if config.gemm_backend == "tcgen05":
             K.gemm_set_l2_prefetch(config.gemm_l2_prefetch)
+        if config.pdl:
+            K.set_pdl(True)
         prev_dtype = torch.get_default_dtype()
         torch.set_default_dtype(torch.bfloat16)
         torch.set_default_device(self.device)

@@ -66,6 +66,7 @@ CASES = [
      INVALID, "bad sizes"),
     ("kvb_gemm_set_l2_prefetch", (-1,), INVALID, "ksteps"),
     ("kvb_gemm_set_l2_prefetch", (65,), INVALID, "ksteps"),
+    ("kvb_set_pdl", (2,), INVALID, "enable"),
 ]
 
 

@@ -2,8 +2,9 @@
 default paths' tests: GEMM K splits whose cluster size is not a power of two
 (the reduction deals the tile's sixteen 8-feature groups unevenly over the
 ranks), the L2 prefetch of the weight stream (kvb_gemm_set_l2_prefetch), the
-tcgen05 GEMM backend inside the model, and pipelined decode
-(ModelRunner.run_async with one step in flight)."""
+tcgen05 GEMM backend inside the model, pipelined decode
+(ModelRunner.run_async with one step in flight) and programmatic dependent
+launch (kvb_set_pdl)."""
 import pytest
 import torch
 
@@ -152,3 +153,21 @@ def test_tcgen05_gemm_backend_in_the_model(tiny_dir):
     prompt_lens = (300, 17, 255, 1)
     same = sum(a[:n + 2] == b[:n + 2] for a, b, n in zip(runs[0], runs[1], prompt_lens))
     assert same >= 3  # prefill token and first decode token of at least 3 of the 4 sequences
+
+
+def test_programmatic_dependent_launch_changes_no_result(tiny_dir):
+    """With every kernel launched as a programmatic dependent (kvb_set_pdl)
+    inside and outside the captured decode graphs, greedy decoding gives the
+    same tokens as plain stream-ordered launches: each kernel waits at its
+    start for the one before it."""
+    from kavor_b200 import _kernels as K_
+
+    runs = []
+    for pdl in (False, True):
+        runner = _runner(tiny_dir, pdl=pdl)
+        try:
+            runs.append(_greedy_decode(runner, False))
+        finally:
+            runner.exit()
+            K_.set_pdl(False)
+    assert runs[0] == runs[1]

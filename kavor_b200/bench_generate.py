@@ -1,7 +1,8 @@
 """Offline generate throughput through the public API, on the workload of the
 reference's own benchmark (benchs/bench.py:8-26).
 
-    python -m kavor_b200.bench_generate [--model Qwen3-0.6B] [--tp 1] [--num-seqs 256]
+    python -m kavor_b200.bench_generate [--model Qwen3-0.6B] [--tp 1] [--num-seqs 256] [--async-decode]
+        [--gemm cublas|tcgen05] [--pdl]
 
 256 sequences of uniform-random token ids in [0, 10000], prompt lengths
 U[100, 1024], max_tokens U[100, 1024] (Python's `random` seeded with 0, drawn
@@ -32,6 +33,9 @@ def main(argv=None) -> int:
     ap.add_argument("--num-seqs", type=int, default=256)
     ap.add_argument("--max-input-len", type=int, default=1024)
     ap.add_argument("--max-output-len", type=int, default=1024)
+    ap.add_argument("--async-decode", action="store_true", help="one decode step in flight (Config.async_decode)")
+    ap.add_argument("--gemm", choices=["cublas", "tcgen05"], default="cublas")
+    ap.add_argument("--pdl", action="store_true")
     a = ap.parse_args(argv)
 
     from kavor_b200 import LLM, SamplingParams
@@ -43,7 +47,7 @@ def main(argv=None) -> int:
               for _ in range(a.num_seqs)]
     model_dir = write_model_dir(os.path.join(tempfile.mkdtemp(prefix="kvb_gen_"), "m"), a.model)
     llm = LLM(model_dir, load_format="dummy", tensor_parallel_size=a.tp, max_model_len=4096,
-              enable_prefix_caching=False)
+              enable_prefix_caching=False, async_decode=a.async_decode, gemm_backend=a.gemm, pdl=a.pdl)
     try:
         llm.generate([[1, 2, 3, 4]], SamplingParams(max_tokens=8), use_tqdm=False)
         t0 = time.perf_counter()
@@ -54,7 +58,7 @@ def main(argv=None) -> int:
     total = sum(sp.max_tokens for sp in params)
     generated = sum(len(o["token_ids"]) for o in out)
     print(json.dumps({"workload": f"offline generate, {a.model}, {a.num_seqs} seqs, prompt/output U[100,1024]",
-                      "tp": a.tp, "total_tokens": total, "generated_tokens": generated, "seconds": dt,
+                      "tp": a.tp, "async_decode": a.async_decode, "gemm": a.gemm, "pdl": a.pdl, "total_tokens": total, "generated_tokens": generated, "seconds": dt,
                       "tok_s": total / dt, "reference_published_tok_s": REFERENCE_PUBLISHED_TOK_S,
                       "reference_hardware": "RTX 4070 Laptop 8 GB (README.md:44-55)"}), flush=True)
     return 0 if generated == total else 1

@@ -6,8 +6,9 @@ in ``model``, "dummy" draws a seeded random checkpoint of the same shapes),
 caches prefixes), ``graph_batch_sizes`` (the decode batch buckets captured
 as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16),
 ``fused_allreduce``, ``gemm_backend`` / ``gemm_l2_prefetch`` (which GEMM
-the projections use, and its L2 prefetch distance) and ``pdl`` (programmatic
-dependent launch of the package's kernels).
+the projections use, and its L2 prefetch distance), ``pdl`` (programmatic
+dependent launch of the package's kernels) and ``async_decode`` (the engine
+keeps one decode step in flight).
 """
 from __future__ import annotations
 
@@ -57,6 +58,7 @@ class Config:
     gemm_backend: str = "cublas"  # projections: "cublas" (F.linear) or "tcgen05" (kvb_gemm_bf16, fused gate-up+SiLU)
     gemm_l2_prefetch: int = 0     # tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads (0 = off)
     pdl: bool = False             # programmatic dependent launch of the package's kernels (kvb_set_pdl)
+    async_decode: bool = False    # LLM.generate: one decode step in flight (engine.pipeline.DecodePipeline)
 
     def __post_init__(self):
         if not os.path.isdir(self.model):

@@ -4,9 +4,10 @@
 llm_engine.py:44-52), builds rank 0's ``ModelRunner`` and the ``Scheduler``;
 ``generate`` adds requests and steps until every sequence finished
 (llm_engine.py:245-272). Prompts are strings (needs a tokenizer in the model
-directory) or token-id lists. With ``profile=True`` every step records
-{prefill, tokens, step_time, forward_time} in ``step_stats`` and finished
-requests land in ``request_stats`` (llm_engine.py:140-181).
+directory) or token-id lists. With ``async_decode=True`` decode steps run
+with one step in flight (``DecodePipeline``). With ``profile=True`` every
+step records {prefill, tokens, step_time, forward_time} in ``step_stats``
+and finished requests land in ``request_stats`` (llm_engine.py:140-181).
 """
 from __future__ import annotations
 
@@ -19,6 +20,7 @@ import torch.multiprocessing as mp
 
 from kavor_b200.config import Config
 from kavor_b200.engine.model_runner import ModelRunner
+from kavor_b200.engine.pipeline import DecodePipeline
 from kavor_b200.engine.scheduler import Scheduler
 from kavor_b200.engine.sequence import Sequence
 from kavor_b200.sampling_params import SamplingParams
@@ -71,6 +73,9 @@ class LLMEngine:
                 eos = config.hf_config.eos_token_id
                 config.eos = eos[0] if isinstance(eos, (list, tuple)) else eos
             self.scheduler = Scheduler(config)
+            # one decode step in flight (Config.async_decode); profiling keeps the step-at-a-time loop
+            self.pipeline = (DecodePipeline(self.scheduler, self.model_runner.call)
+                             if config.async_decode and not config.profile else None)
         except BaseException:
             self.exit()
             raise
@@ -116,6 +121,8 @@ class LLMEngine:
         return seq.seq_id
 
     def step(self):
+        if self.pipeline is not None:
+            return [(s.seq_id, s.completion_token_ids) for s in self.pipeline.step()]
         seqs, is_prefill = self.scheduler.schedule()
         token_ids = self.model_runner.call("run", seqs, is_prefill)
         if is_prefill:
@@ -151,6 +158,8 @@ class LLMEngine:
         return [(s.seq_id, s.completion_token_ids) for s in seqs if s.is_finished]
 
     def is_finished(self) -> bool:
+        if self.pipeline is not None:
+            return self.pipeline.is_finished()
         return self.scheduler.is_finished()
 
     def generate(self, inputs, sampling_params: SamplingParams | list[SamplingParams], use_tqdm: bool = True):

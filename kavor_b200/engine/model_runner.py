@@ -170,6 +170,10 @@ class DecodeBuffers:
         self.copied: list[torch.cuda.Event | None] = [None] * self.MIRRORS
         self.sampled = torch.zeros(max_bs, dtype=torch.int64, device=device)
         self.tokens_host = [torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True) for _ in range(2)]
+        # a chained step's gather map: row i takes the previous step's sample chain[i]
+        self.chain_host = [torch.zeros(max_bs, dtype=torch.int64, device="cpu", pin_memory=True) for _ in range(2)]
+        self.chain_copied: list[torch.cuda.Event | None] = [None, None]
+        self.chain_dev = torch.zeros(max_bs, dtype=torch.int64, device=device)
 
     def fill(self, meta: dict, temperatures: np.ndarray, bucket: int, mirror: int = 0) -> None:
         if self.copied[mirror] is not None:  # the previous copy out of this mirror has been read
@@ -537,10 +541,11 @@ class ModelRunner:
         bs = self._decode_launch(seqs, temps, mirror=0, chain=False)
         return self.decode_buffers.sampled[:bs].tolist()
 
-    def _decode_launch(self, seqs: list[Sequence], temps: np.ndarray, mirror: int, chain: bool) -> int:
+    def _decode_launch(self, seqs: list[Sequence], temps: np.ndarray, mirror: int, chain) -> int:
         """Upload one decode step's metadata (through pinned mirror `mirror`),
         optionally take the input tokens from the previous step's samples on
-        the device, and launch the step (graph replay, or eager)."""
+        the device (chain True: row i from row i; a list: row i from row
+        chain[i]), and launch the step (graph replay, or eager)."""
         meta = decode_metadata(seqs, self.block_size)
         bs = len(seqs)
         self._ensure_decode_buffers()
@@ -550,8 +555,17 @@ class ModelRunner:
                                f"runner's {buf.max_bs} x {buf.max_blocks}")
         bucket = next((b for b in getattr(self, "graph_bs", []) if b >= bs), bs)
         buf.fill(meta, temps, bucket, mirror)
-        if chain:
+        if chain is True:
             buf.d["input_ids"][:bs].copy_(buf.sampled[:bs])
+        elif chain:
+            k = mirror - 1
+            if buf.chain_copied[k] is not None:
+                buf.chain_copied[k].synchronize()
+            buf.chain_host[k][:bs] = torch.as_tensor(chain, dtype=torch.int64)
+            buf.chain_dev[:bs].copy_(buf.chain_host[k][:bs], non_blocking=True)
+            buf.chain_copied[k] = torch.cuda.Event()
+            buf.chain_copied[k].record()
+            torch.index_select(buf.sampled, 0, buf.chain_dev[:bs], out=buf.d["input_ids"][:bs])
         graph = self.graphs.get(bucket)
         if graph is not None:
             graph.replay()
@@ -566,13 +580,15 @@ class ModelRunner:
         return bs
 
     @torch.inference_mode()
-    def run_async(self, seqs: list[Sequence], chain: bool = False) -> PendingDecode | None:
+    def run_async(self, seqs: list[Sequence], chain: bool | list[int] = False) -> PendingDecode | None:
         """One decode step, issued without waiting for it (no reference
         counterpart; ``run`` is the reference's synchronous call). With
         ``chain``, every sequence's input token is the token the previous
-        ``run_async`` step sampled for it, copied on the device: the same
-        sequences in the same order, each grown on the host since by one
-        placeholder token (its value is not read). Returns a PendingDecode,
+        ``run_async`` step sampled for it, copied on the device: True when the
+        batch is the previous step's sequences in the same order, or a list
+        giving each sequence's row in the previous step's batch; each sequence
+        grew on the host since by one placeholder token (its value is not
+        read). Returns a PendingDecode,
         whose ``result()`` must be read before the step after the next one is
         issued — except on a TP worker driven through the mailbox by rank 0,
         which returns None (every rank samples the same tokens; rank 0 reads
@@ -584,8 +600,11 @@ class ModelRunner:
         prev = self._pending[k]
         if prev is not None and not prev.done and not mailbox_worker:
             raise RuntimeError("run_async: the result of the step issued two calls ago has not been read")
-        if chain and len(seqs) != self._async_bs:
+        if chain is True and len(seqs) != self._async_bs:
             raise RuntimeError(f"run_async: a chained step needs the previous step's {self._async_bs} sequences")
+        if isinstance(chain, list) and (len(chain) != len(seqs) or not all(0 <= i < self._async_bs for i in chain)):
+            raise RuntimeError(f"run_async: the chain map must give every sequence a row of the previous "
+                               f"{self._async_bs}-sequence step")
         temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
         bs = self._decode_launch(seqs, temps, mirror=1 + k, chain=chain)
         self._async_bs = bs

@@ -297,3 +297,84 @@ def test_pipelined_decode_ends_like_the_synchronous_one(make_seq, steps):
         advance_decode(_FakeRunner(), seqs, bm, steps, pipelined=pipelined)
         runs.append([(s.token_ids, s.last_token, s.block_table, s.num_cached_tokens, len(s)) for s in seqs])
     assert runs[0] == runs[1]
+
+
+class _FakeEngineRunner:
+    """Host model of the runner behind the engine: the 'device' samples
+    (7 x input token + 13 x position) mod 50 for every step, prefill chunks
+    included; token 3 is the end of sequence. run_async keeps its samples on
+    the 'device' and a chained step reads its inputs from them (row map or
+    same order), never from the host's placeholder."""
+
+    VOCAB = 50
+
+    def __init__(self):
+        self.device_sampled = None
+
+    def _tok(self, inp, pos):
+        return (7 * inp + 13 * pos) % self.VOCAB
+
+    def call(self, method, *args):
+        return getattr(self, method)(*args)
+
+    def run(self, seqs, is_prefill):
+        if is_prefill:
+            ends = [s.num_cached_tokens + s.num_scheduled_tokens - 1 for s in seqs]
+            return [self._tok(s.token_ids[e], e) for s, e in zip(seqs, ends)]
+        return [self._tok(s.last_token, len(s) - 1) for s in seqs]
+
+    def run_async(self, seqs, chain=False):
+        if chain is True:
+            inputs = list(self.device_sampled)
+        elif chain:
+            inputs = [self.device_sampled[i] for i in chain]
+        else:
+            inputs = [s.last_token for s in seqs]
+        assert all(t >= 0 for t in inputs), "a placeholder reached the model"
+        self.device_sampled = [self._tok(t, len(s) - 1) for t, s in zip(inputs, seqs)]
+        return _FakePending(self.device_sampled)
+
+
+def _engine_outputs(make_config, make_seq, pipelined, num_blocks, arrivals):
+    from kavor_b200.engine.pipeline import DecodePipeline
+
+    sched = Scheduler(make_config(eos=3, num_kvcache_blocks=num_blocks, max_num_batched_tokens=24, max_num_seqs=6))
+    runner = _FakeEngineRunner()
+    pipe = DecodePipeline(sched, runner.call) if pipelined else None
+    finished, step = {}, 0
+    pending = list(arrivals)
+    while pending or not (pipe.is_finished() if pipe else sched.is_finished()):
+        while pending and pending[0][0] <= step:  # requests arriving while others run
+            _, prompt, max_tokens, ignore_eos = pending.pop(0)
+            sched.add(make_seq(prompt, max_tokens=max_tokens, ignore_eos=ignore_eos))
+        step += 1
+        if pipe is not None:
+            done = pipe.step()
+        else:
+            if sched.is_finished():
+                continue
+            seqs, is_prefill = sched.schedule()
+            sched.postprocess(seqs, runner.run(seqs, is_prefill), is_prefill)
+            done = [s for s in seqs if s.is_finished]
+        for s in done:
+            assert s.seq_id not in finished
+            finished[s.seq_id] = (s.prompt_token_ids, s.completion_token_ids)
+    bm = sched.block_manager
+    assert len(bm.free_block_ids) == num_blocks and not bm.used_block_ids
+    return sorted(finished.values())
+
+
+@pytest.mark.parametrize("num_blocks", [64, 12])  # 12 blocks of 4 tokens: decode preempts
+def test_decode_pipeline_gives_the_step_at_a_time_outputs(make_seq, make_config, num_blocks):
+    """DecodePipeline (one decode step in flight, placeholders, tokens chained
+    on the device, end-of-sequence seen one step late) returns exactly the
+    completions of the schedule -> run -> postprocess loop: prompts of
+    different lengths (chunked prefill), max_tokens and end-of-sequence
+    finishes, requests arriving mid-run, and a pool small enough to preempt."""
+    arrivals = [(0, [5, 9, 11, 2, 8, 30], 9, False), (0, list(range(1, 20)), 14, False), (0, [4], 6, True),
+                (0, [17, 17, 17, 17, 17], 20, False), (3, [6, 7], 5, False), (9, list(range(21, 31)), 11, True),
+                (9, [12, 1, 44], 25, False), (15, [2], 7, False)]
+    sync = _engine_outputs(make_config, make_seq, False, num_blocks, arrivals)
+    piped = _engine_outputs(make_config, make_seq, True, num_blocks, arrivals)
+    assert piped == sync
+    assert any(c and c[-1] == 3 for _, c in sync)  # some sequence ended on its end-of-sequence token

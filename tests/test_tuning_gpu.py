@@ -3,8 +3,8 @@ default paths' tests: GEMM K splits whose cluster size is not a power of two
 (the reduction deals the tile's sixteen 8-feature groups unevenly over the
 ranks), the L2 prefetch of the weight stream (kvb_gemm_set_l2_prefetch), the
 tcgen05 GEMM backend inside the model, pipelined decode
-(ModelRunner.run_async with one step in flight) and programmatic dependent
-launch (kvb_set_pdl)."""
+(ModelRunner.run_async with one step in flight, and the engine's
+DecodePipeline) and programmatic dependent launch (kvb_set_pdl)."""
 import pytest
 import torch
 
@@ -171,3 +171,29 @@ def test_programmatic_dependent_launch_changes_no_result(tiny_dir):
             runner.exit()
             K_.set_pdl(False)
     assert runs[0] == runs[1]
+
+
+def test_async_decode_engine_gives_the_same_generations(tiny_dir):
+    """LLM.generate with one decode step in flight (Config.async_decode)
+    returns the generations of the step-at-a-time engine: sampled at
+    temperature 0.6 with ignore_eos, the steps see the same batches in the
+    same order and the same sampler seeds."""
+    import torch.distributed as dist
+
+    from kavor_b200 import LLM, SamplingParams
+
+    prompts = [[(3 * j + i) % 4000 + 1 for j in range(n)] for i, n in enumerate((300, 17, 700, 1, 64))]
+    params = [SamplingParams(temperature=0.6, max_tokens=m, ignore_eos=True) for m in (9, 30, 4, 17, 12)]
+    outs = []
+    for async_decode in (False, True):
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        llm = LLM(tiny_dir, load_format="dummy", seed=1, max_model_len=2048, max_num_seqs=8,
+                  max_num_batched_tokens=512, num_kvcache_blocks=32, rdzv_port=29577 + int(async_decode),
+                  async_decode=async_decode)
+        try:
+            outs.append([o["token_ids"] for o in llm.generate(prompts, params, use_tqdm=False)])
+        finally:
+            llm.exit()
+    assert [len(o) for o in outs[1]] == [9, 30, 4, 17, 12]
+    assert outs[0] == outs[1]

@@ -135,24 +135,61 @@ def test_pipelined_decode_gives_the_synchronous_tokens(tiny_dir):
     assert piped == sync
 
 
-def test_tcgen05_gemm_backend_in_the_model(tiny_dir):
-    """The model with every projection on kvb_gemm_bf16 (gate-up + SiLU fused)
-    decodes greedily like the cuBLAS model (logits differ by summation order
-    only, so the tokens may part at a near-tie: compare the first steps)."""
-    from kavor_b200.layers.linear import set_gemm_backend
+@pytest.mark.parametrize("prefetch", [0, 8])
+def test_tcgen05_gemm_backend_replays_reference_greedy(prefetch):
+    """The tiny Qwen3 with every projection on kvb_gemm_bf16 (the MLP's gate-up
+    + SiLU in kvb_gemm_silu_bf16), teacher-forced on the reference model's
+    prefill + 8 greedy decode steps: logits cosine >= 0.999 at every step and
+    the greedy token wherever the reference's top two logits are more than
+    two bf16 ulps apart; the L2 prefetch of the weights changes nothing."""
+    import cases
+    from conftest import GOLDEN
 
-    runs = []
-    for backend, pf in (("cublas", 0), ("tcgen05", 0), ("tcgen05", 8)):
-        runner = _runner(tiny_dir, gemm_backend=backend, gemm_l2_prefetch=pf)
+    from kavor_b200 import _kernels as K_
+    from kavor_b200.layers.linear import set_gemm_backend
+    from kavor_b200.models import AutoModelForCausalLM, _assign
+    from kavor_b200.utils.context import reset_context, set_context
+
+    dev = torch.device("cuda", 0)
+    cfg = cases.hf_config(cases.TINY)
+    torch.set_default_dtype(torch.bfloat16)
+    torch.set_default_device(dev)
+    try:
+        model = AutoModelForCausalLM.model_class(cfg)(cfg)
+    finally:
+        torch.set_default_device("cpu")
+        torch.set_default_dtype(torch.float32)
+    loaded = set()
+    for name, t in cases.checkpoint(cases.TINY, seed=5).items():
+        _assign(model, name, t.to(dev), model.packed_modules_mapping, loaded)
+    for lyr in model.model.layers:
+        pool = torch.zeros(8, 2, 256, 2, 128, dtype=torch.bfloat16, device=dev)
+        lyr.self_attn.attn.k_cache = [pool[:, 0]]
+        lyr.self_attn.attn.v_cache = [pool[:, 1]]
+
+    def step(b):
+        b = {k: v.to(dev) if isinstance(v, torch.Tensor) else v for k, v in b.items()}
+        if b["is_prefill"]:
+            n = int((b["cu_seqlens"][1:] - b["cu_seqlens"][:-1]).max())
+            set_context(True, b["cu_seqlens"], b["cu_seqlens"], n, n, b["slot_mapping"])
+        else:
+            set_context(False, slot_mapping=b["slot_mapping"], context_lens=b["context_lens"],
+                        block_tables=b["block_tables"])
         try:
-            runs.append(_greedy_decode(runner, False, steps=3))
+            with torch.inference_mode():
+                return model.compute_logits(model(b["input_ids"], b["positions"]))
         finally:
-            runner.exit()
-            set_gemm_backend("cublas")
-    assert runs[1] == runs[2]  # the prefetch changes no bit
-    prompt_lens = (300, 17, 255, 1)
-    same = sum(a[:n + 2] == b[:n + 2] for a, b, n in zip(runs[0], runs[1], prompt_lens))
-    assert same >= 3  # prefill token and first decode token of at least 3 of the 4 sequences
+            reset_context()
+
+    set_gemm_backend("tcgen05")
+    K_.gemm_set_l2_prefetch(prefetch)
+    try:
+        gold = torch.load(GOLDEN / "tiny_model_golden.pt", weights_only=False)
+        checked = sum(cases.check_greedy_step(logits, rec) for logits, rec in cases.replay(gold, step))
+    finally:
+        set_gemm_backend("cublas")
+        K_.gemm_set_l2_prefetch(0)
+    assert checked >= 13
 
 
 def test_programmatic_dependent_launch_changes_no_result(tiny_dir):

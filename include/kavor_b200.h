@@ -223,6 +223,19 @@ int kvb_gemm_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, v
  * plan[2] work units, plan[3] CTAs. */
 int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan);
 
+/* y[M, N] = x[M, K] * w[N, K]^T on CTA pairs (tcgen05 cta_group::2; no
+ * reference counterpart beyond the F.linear it computes): each pair of a
+ * thread-block cluster multiplies 256 weight rows (128 per CTA) by a token
+ * tile of 64, 128 or 256 tokens (half per CTA) with one MMA per 16-wide K
+ * step, and `splits` pairs (1..8, 0 = chosen for one CTA per SM) share K
+ * through a distributed-shared-memory reduction in a fixed order. Same
+ * operand rules as kvb_gemm_bf16; no workspace. */
+int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N,
+                       int K, int splits, void* stream);
+/* The pair GEMM's plan for this shape (host only): plan[0] token tile,
+ * plan[1] K splits, plan[2] tiles, plan[3] CTAs. */
+int kvb_gemm_pair_plan(int M, int N, int K, int splits, int* plan);
+
 /* Process-wide tuning of kvb_gemm_bf16 / kvb_gemm_silu_bf16 (no reference
  * counterpart): the producer asks L2 for the weight K-steps `ksteps` ahead of
  * its TMA loads (cp.async.bulk.prefetch.tensor; 0 = off, the default; at most

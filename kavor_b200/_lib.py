@@ -42,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "kvb_gemm_bf16": [P, L, P, L, P, L, I, I, I, I, P, c_size_t, P],
     "kvb_gemm_plan": [I, I, I, I, I, POINTER(c_int)],
     "kvb_gemm_set_l2_prefetch": [I],
+    "kvb_gemm_pair_bf16": [P, L, P, L, P, L, I, I, I, I, P],
+    "kvb_gemm_pair_plan": [I, I, I, I, POINTER(c_int)],
     "kvb_set_pdl": [I],
     "kvb_gemm_silu_workspace_size": [I, I, I, I, POINTER(c_size_t)],
     "kvb_gemm_silu_bf16": [P, L, P, L, P, L, I, I, I, I, P, c_size_t, P],
@@ -62,7 +64,7 @@ _lib: ctypes.CDLL | None = None
 
 # Entry points that only query or report (everything else launches kernels).
 _QUERIES = {"kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
-            "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch", "kvb_set_pdl", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach", "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
+            "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch", "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach", "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
             "kvb_comm_data_buffer", "kvb_comm_destroy"}
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.

@@ -37,12 +37,14 @@ int read_device_error_prefill(unsigned*, int);
 int read_device_error_sampler(unsigned*, int);
 int read_device_error_gemm(unsigned*, int);
 int read_device_error_allreduce(unsigned*, int);
+int read_device_error_gemm_pair(unsigned*, int);
 int set_pdl_trigger_elementwise(int);
 int set_pdl_trigger_decode(int);
 int set_pdl_trigger_prefill(int);
 int set_pdl_trigger_sampler(int);
 int set_pdl_trigger_gemm(int);
 int set_pdl_trigger_allreduce(int);
+int set_pdl_trigger_gemm_pair(int);
 
 }  // namespace kvb
 
@@ -57,7 +59,8 @@ extern "C" int kvb_device_error(unsigned* bits, int clear) {
   unsigned acc = 0, w = 0;
   int (*readers[])(unsigned*, int) = {kvb::read_device_error_elementwise, kvb::read_device_error_decode,
                                       kvb::read_device_error_prefill, kvb::read_device_error_sampler,
-                                      kvb::read_device_error_gemm, kvb::read_device_error_allreduce};
+                                      kvb::read_device_error_gemm, kvb::read_device_error_allreduce,
+                                      kvb::read_device_error_gemm_pair};
   for (auto fn : readers) {
     int rc = fn(&w, clear);
     if (rc) return rc;
@@ -71,7 +74,7 @@ extern "C" int kvb_set_pdl(int enable) {
   if (enable != 0 && enable != 1) return kvb::set_error(kvb::kInvalid, "kvb_set_pdl: enable must be 0 or 1");
   int (*setters[])(int) = {kvb::set_pdl_trigger_elementwise, kvb::set_pdl_trigger_decode,
                            kvb::set_pdl_trigger_prefill, kvb::set_pdl_trigger_sampler, kvb::set_pdl_trigger_gemm,
-                           kvb::set_pdl_trigger_allreduce};
+                           kvb::set_pdl_trigger_allreduce, kvb::set_pdl_trigger_gemm_pair};
   for (auto fn : setters) {
     int rc = fn(enable);
     if (rc) return rc;

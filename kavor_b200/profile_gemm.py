@@ -2,11 +2,12 @@
 plan and every forced K split), kvb_gemm_silu_bf16 for the gate-up shapes, and
 cuBLAS (torch.matmul) on the same operands.
 
-    python -m kavor_b200.profile_gemm [M,M,...] [--splits 1,2,3,4,8,16] [--l2-prefetch 0,4]
+    python -m kavor_b200.profile_gemm [M,M,...] [--splits 1,2,3,4,8,16] [--l2-prefetch 0,4] [--pair]
 
 (default M 1,64,256; K splits 1,2,4,8,16; L2 prefetch distance 0). Every
 variant runs at every L2 prefetch distance given (kvb_gemm_set_l2_prefetch);
-labels carry a "_pfN" suffix when N > 0.
+labels carry a "_pfN" suffix when N > 0. --pair adds the CTA-pair kernel
+(kvb_gemm_pair_bf16): "pair_auto" and "pair_sN" for K splits N <= 8.
 
 Shapes: QKV, O, gate-up, down and LM head of Qwen3-8B at TP=1 and TP=8. Each
 timing is one replay of a CUDA graph of 20 launches (device time, CUDA events),
@@ -49,6 +50,7 @@ def main(argv=None) -> int:
     ap.add_argument("ms", nargs="?", default="1,64,256")
     ap.add_argument("--splits", default="1,2,4,8,16")
     ap.add_argument("--l2-prefetch", default="0")
+    ap.add_argument("--pair", action="store_true")
     a = ap.parse_args(argv)
     split_list = [int(v) for v in a.splits.split(",")]
     pf_list = [int(v) for v in a.l2_prefetch.split(",")]
@@ -93,6 +95,16 @@ def main(argv=None) -> int:
                         t = _timeit(lambda i: K.gemm_silu(x, ws[i % len(ws)], out=og, splits=splits))
                         res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"]]
             K.gemm_set_l2_prefetch(0)
+            if a.pair:
+                for splits in [0] + [s for s in split_list if s <= 8]:
+                    p = K.gemm_pair_plan(M, N, Kd, splits)
+                    if splits and p["splits"] != splits:
+                        continue
+                    label = "pair_auto" if splits == 0 else f"pair_s{splits}"
+                    K.gemm_pair(x, ws[0], out=out, splits=splits)
+                    err = (out.float() - ref.float()).abs().max().item()
+                    t = _timeit(lambda i: K.gemm_pair(x, ws[i % len(ws)], out=out, splits=splits))
+                    res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"], round(err, 4)]
             t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
             res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
             res["device_error_bits"] = _lib.device_error(clear=True)

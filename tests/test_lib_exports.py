@@ -115,6 +115,27 @@ def test_gemm_forced_splits_of_any_cluster_size(lib):
                 assert p == K.gemm_plan(M, N, Kd)
 
 
+def test_gemm_pair_plans(lib):
+    """Host-side plan of the CTA-pair GEMM (no launch): token tile 64 / 128 /
+    256 by batch, 256-row weight tiles, K splits that keep each tile's
+    2 x splits CTAs within one CTA per SM, every part non-empty."""
+    import math
+
+    from kavor_b200 import _kernels as K
+
+    for M in (1, 7, 64, 65, 128, 200, 256, 300, 2048):
+        for N, Kd in ((768, 4096), (6144, 4096), (4096, 512), (4096, 12288), (151936, 4096), (1000, 1024)):
+            p = K.gemm_pair_plan(M, N, Kd)
+            mt = 64 if M <= 64 else (128 if M <= 128 else 256)
+            tiles = math.ceil(N / 256) * math.ceil(M / mt)
+            kb = math.ceil(Kd / 64)
+            assert p["mt"] == mt and p["tiles"] == tiles and p["ctas"] == 2 * tiles * p["splits"]
+            assert 1 <= p["splits"] <= 8 and (p["splits"] - 1) * math.ceil(kb / p["splits"]) < kb
+            assert p["splits"] == 1 or p["ctas"] <= 148
+    assert K.gemm_pair_plan(256, 6144, 4096)["splits"] == 3  # Qwen3-8B QKV at decode batch 256: 144 CTAs
+    assert K.gemm_pair_plan(256, 6144, 4096, splits=5)["splits"] == 5
+
+
 def test_allreduce_plan_matches_the_documented_choice(lib):
     """Host-side mode choice of the fused all-reduce (no launch): peer one-shot
     at 2 ranks, switch one-shot below 8 rows per rank and switch two-shot from

@@ -57,7 +57,7 @@ def parse_args(argv=None):
     ap.add_argument("--context", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--gemm", choices=["cublas", "tcgen05"], default="cublas",
+    ap.add_argument("--gemm", choices=["cublas", "tcgen05", "tcgen05_pair"], default="cublas",
                     help="GEMM of the projections (Config.gemm_backend)")
     ap.add_argument("--gemm-l2-prefetch", type=int, default=0,
                     help="tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads")

@@ -34,7 +34,7 @@ def main(argv=None) -> int:
     ap.add_argument("--max-input-len", type=int, default=1024)
     ap.add_argument("--max-output-len", type=int, default=1024)
     ap.add_argument("--async-decode", action="store_true", help="one decode step in flight (Config.async_decode)")
-    ap.add_argument("--gemm", choices=["cublas", "tcgen05"], default="cublas")
+    ap.add_argument("--gemm", choices=["cublas", "tcgen05", "tcgen05_pair"], default="cublas")
     ap.add_argument("--pdl", action="store_true")
     a = ap.parse_args(argv)
 

@@ -6,9 +6,10 @@ gate/up rows [gate | up] per rank), row-parallel layers split the input
 columns and all-reduce the partial products (bias added on rank 0 only).
 All projections go through ``linear()``, the single GEMM entry point of the
 package. Which GEMM runs is a process-wide choice (``set_gemm_backend``):
-"cublas" (torch's F.linear, the reference's own GEMM; the default) or
+"cublas" (torch's F.linear, the reference's own GEMM; the default),
 "tcgen05" (this package's kernel, kvb_gemm_bf16, with the gate-up projection
-and SiluAndMul fused into kvb_gemm_silu_bf16 by the MLP).
+and SiluAndMul fused into kvb_gemm_silu_bf16 by the MLP) or "tcgen05_pair"
+(the CTA-pair kernel, kvb_gemm_pair_bf16, for every projection).
 """
 from __future__ import annotations
 
@@ -24,7 +25,7 @@ def divide(numerator: int, denominator: int) -> int:
     return numerator // denominator
 
 
-GEMM_BACKENDS = ("cublas", "tcgen05")
+GEMM_BACKENDS = ("cublas", "tcgen05", "tcgen05_pair")
 _GEMM_BACKEND = "cublas"
 
 
@@ -42,10 +43,10 @@ def gemm_backend() -> str:
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x W^T (+ b) in bf16 with fp32 accumulation."""
-    if _GEMM_BACKEND == "tcgen05":
+    if _GEMM_BACKEND != "cublas":
         from kavor_b200 import _kernels as K
 
-        y = K.gemm(x, weight, out=out)
+        y = (K.gemm if _GEMM_BACKEND == "tcgen05" else K.gemm_pair)(x, weight, out=out)
         if bias is not None:
             y.add_(bias)
         return y

@@ -78,17 +78,20 @@ def _model(cfg):
 CASES = [("qwen3", "tiny_model_golden.pt")] + [(f, f"{f}_tiny_golden.pt") for f in cases.FAMILIES]
 
 
-@pytest.fixture(params=["cublas", "tcgen05"])
+@pytest.fixture(params=["cublas", "tcgen05", "tcgen05_pair"])
 def gemm_backend(request, monkeypatch):
-    """Both GEMM backends of linear(): torch's F.linear, or the package's
+    """Every GEMM backend of linear(): torch's F.linear, or the package's
     kernel entry points (replaced here by the oracle's linear, with the gate-up
     + SiLU fusion of the MLP as silu_mul(linear))."""
     from kavor_b200 import _kernels as K
     from kavor_b200.layers import linear as L
 
-    if request.param == "tcgen05":
-        monkeypatch.setattr(K, "gemm", lambda x, w, out=None, splits=0: ops.linear(x, w) if out is None
-                            else out.copy_(ops.linear(x, w)))
+    def gemm(x, w, out=None, splits=0):
+        return ops.linear(x, w) if out is None else out.copy_(ops.linear(x, w))
+
+    if request.param != "cublas":
+        monkeypatch.setattr(K, "gemm", gemm)
+        monkeypatch.setattr(K, "gemm_pair", gemm)
         monkeypatch.setattr(K, "gemm_silu", lambda x, w, out=None, splits=0: ops.silu_mul(ops.linear(x, w)))
     L.set_gemm_backend(request.param)
     yield request.param

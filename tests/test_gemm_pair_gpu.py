@@ -3,7 +3,7 @@ reference and cuBLAS over decode and prefill shapes of the Qwen3 projections,
 ragged M and N, forced K splits, NaN-filled outputs and determinism.
 
 The kernel has not run on a GPU yet: these tests run only with
-KVB_RUN_NEW_KERNELS=1 until its first run on a B200 has passed."""
+KVB_GPU_PENDING=1 until their first run on a B200 has passed."""
 import os
 
 import pytest
@@ -11,8 +11,8 @@ import torch
 import torch.nn.functional as F
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("KVB_RUN_NEW_KERNELS") != "1",
-                                 reason="first GPU run of the CTA-pair GEMM pending (KVB_RUN_NEW_KERNELS=1)")]
+              pytest.mark.skipif(os.environ.get("KVB_GPU_PENDING") != "1",
+                                 reason="first GPU run of the CTA-pair GEMM pending (KVB_GPU_PENDING=1)")]
 DEV = "cuda"
 
 

@@ -14,6 +14,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -45,6 +46,37 @@ enum DeviceError : unsigned {
 // Host-side error message helpers (defined in capi.cu).
 int set_error(int status, const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* where);
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry
+// point (the library links no libcuda); NULL when the driver lacks it.
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// SM count of the current device, cached per device (148, the B200's, when it
+// cannot be read: host-only planning on a machine without a GPU).
+inline int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) cudaGetLastError();
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
 
 // Spin budget for every device-side wait: ~2^31 SM cycles (about a second at
 // 1.9 GHz). Waits that exceed it set kErrTimeout and give up.

@@ -291,18 +291,6 @@ __global__ void decode_merge_kernel(const float* __restrict__ part_o, const floa
   out[(int64_t)b * o_st + (int64_t)h * o_sh + d] = __float2bfloat16_rn(W > 0.f ? O / W : 0.f);
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 int encode_kv_map(CUtensorMap* map, const void* base, int64_t num_blocks, int64_t block_stride, int block_size,
                   int hkv) {
   auto enc = tensor_map_encoder();

@@ -468,20 +468,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
-  auto enc = encoder();
+  auto enc = tensor_map_encoder();
   if (!enc) return set_error(kNoEncoder, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
@@ -497,18 +485,6 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
 // K-steps of weight the producer asks L2 for ahead of its TMA loads
 // (kvb_gemm_set_l2_prefetch; 0 = off).
 std::atomic<int> g_l2_prefetch{0};
-
-int sm_count() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) cudaGetLastError();
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
 
 struct Plan {
   int mt, n_tiles, m_tiles, splits, kb_total, kb_per_split, units, grid;
@@ -550,7 +526,7 @@ Plan finish_plan(int M, int N, int K, int mt, int per_sm, int splits) {
   p.splits = splits;
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.units = p.n_tiles * p.m_tiles * p.splits;
-  const int slots = sm_count() * per_sm;
+  const int slots = device_sm_count() * per_sm;
   p.grid = (p.splits > 1 || p.units < slots) ? p.units : slots;
   return p;
 }
@@ -565,7 +541,7 @@ Plan finish_plan(int M, int N, int K, int mt, int per_sm, int splits) {
 // tokens and the output.
 double plan_cost(const Plan& p, int M, int N, int K, int per_sm, int slabs) {
   const double clk = 1.9e3;  // cycles per us
-  const int nsm = sm_count();
+  const int nsm = device_sm_count();
   const double t_mma = 4.0 * slabs * 128.0 * (p.mt < 32 ? 32 : p.mt) / 256.0 / clk;
   const double kb_bytes = slabs * (double)kABytes + (double)p.mt * kBK * 2;
   const double t_tma = kb_bytes / (per_sm == 2 ? 120e3 : 200e3);

@@ -245,20 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-PFN_cuTensorMapEncodeTiled_v12000 encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
-  auto enc = encoder();
+  auto enc = tensor_map_encoder();
   if (!enc) return set_error(kNoEncoder, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
@@ -269,18 +257,6 @@ int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, 
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(kEncode, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
   return kOk;
-}
-
-int sm_count() {
-  static int cached[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) cudaGetLastError();
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
 }
 
 struct PairPlan {
@@ -306,7 +282,7 @@ PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
   p.m_tiles = (M + p.mt - 1) / p.mt;
   p.kb_total = (K + kBK - 1) / kBK;
   const int tiles = p.n_tiles * p.m_tiles;
-  int s = splits_req > 0 ? splits_req : sm_count() / (2 * tiles);
+  int s = splits_req > 0 ? splits_req : device_sm_count() / (2 * tiles);
   s = s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
   auto valid = [&](int v) {
     if (v > p.kb_total) return false;

@@ -608,23 +608,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 prefill_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // rows of `heads` x 128 bf16 (head stride `sh`, row stride `st`, elements): box
 // {64 dims, 1 head, 128 rows}; 4-D form for the paged cache: {128, heads,
 // block_size, num_blocks} with block stride `bst`.
 int encode_rows(CUtensorMap* map, const void* base, int heads, int64_t rows, int64_t sh, int64_t st) {
-  auto enc = prefill_encoder();
+  auto enc = tensor_map_encoder();
   if (!enc) return set_error(kNoEncoder, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[3] = {(cuuint64_t)kHD, (cuuint64_t)heads, (cuuint64_t)rows};
   const cuuint64_t strides[2] = {(cuuint64_t)sh * 2, (cuuint64_t)st * 2};
@@ -638,7 +626,7 @@ int encode_rows(CUtensorMap* map, const void* base, int heads, int64_t rows, int
 }
 
 int encode_pages(CUtensorMap* map, const void* base, int hkv, int block_size, int64_t num_blocks, int64_t bst) {
-  auto enc = prefill_encoder();
+  auto enc = tensor_map_encoder();
   if (!enc) return set_error(kNoEncoder, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[4] = {(cuuint64_t)kHD, (cuuint64_t)hkv, (cuuint64_t)block_size, (cuuint64_t)num_blocks};
   const cuuint64_t strides[3] = {(cuuint64_t)kHD * 2, (cuuint64_t)hkv * kHD * 2, (cuuint64_t)bst * 2};

@@ -272,9 +272,15 @@ bool landing_fits(int mt, int splits) {
 }
 
 // Token tile: the smallest of 64 / 128 / 256 that holds the batch (256 beyond).
-// K split (pairs per tile): as many as keep every tile's 2 x splits CTAs
-// within one CTA per SM, at most 8, every part non-empty and the reduction
-// inside the ring; splits_req > 0 asks for that split instead.
+// K split (pairs per tile, 1..8, every part non-empty, the reduction inside
+// the ring): the one with the fewest K-steps on the critical path, counting
+// waves of one CTA per SM — ceil(2 x tiles x splits / SMs) x (ceil(K-steps /
+// splits) + a reduction worth kReduceSteps K-steps when split); e.g. 96
+// gate-up tiles: 3 splits, 4 waves x (22 + 4) steps, beat 2 waves x 64; ties
+// go to the smaller split. splits_req > 0 asks for that split instead
+// (reduced until valid).
+constexpr int kReduceSteps = 4;
+
 PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
   PairPlan p;
   p.mt = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
@@ -282,14 +288,28 @@ PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
   p.m_tiles = (M + p.mt - 1) / p.mt;
   p.kb_total = (K + kBK - 1) / kBK;
   const int tiles = p.n_tiles * p.m_tiles;
-  int s = splits_req > 0 ? splits_req : device_sm_count() / (2 * tiles);
-  s = s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
   auto valid = [&](int v) {
     if (v > p.kb_total) return false;
     const int per = (p.kb_total + v - 1) / v;
     return (v - 1) * per < p.kb_total && landing_fits(p.mt, v);
   };
-  while (s > 1 && !valid(s)) --s;
+  int s = 1;
+  if (splits_req > 0) {
+    s = splits_req > kMaxSplits ? kMaxSplits : splits_req;
+    while (s > 1 && !valid(s)) --s;
+  } else {
+    const int64_t nsm = device_sm_count();
+    int64_t best = -1;
+    for (int v = 1; v <= kMaxSplits; ++v) {
+      if (v > 1 && !valid(v)) continue;
+      const int64_t waves = (2 * (int64_t)tiles * v + nsm - 1) / nsm;
+      const int64_t cost = waves * ((p.kb_total + v - 1) / v + (v > 1 ? kReduceSteps : 0));
+      if (best < 0 || cost < best) {
+        best = cost;
+        s = v;
+      }
+    }
+  }
   p.splits = s;
   p.kb_per_split = (p.kb_total + s - 1) / s;
   p.ctas = tiles * 2 * s;

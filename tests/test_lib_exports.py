@@ -131,8 +131,16 @@ def test_gemm_pair_plans(lib):
             kb = math.ceil(Kd / 64)
             assert p["mt"] == mt and p["tiles"] == tiles and p["ctas"] == 2 * tiles * p["splits"]
             assert 1 <= p["splits"] <= 8 and (p["splits"] - 1) * math.ceil(kb / p["splits"]) < kb
-            assert p["splits"] == 1 or p["ctas"] <= 148
-    assert K.gemm_pair_plan(256, 6144, 4096)["splits"] == 3  # Qwen3-8B QKV at decode batch 256: 144 CTAs
+            # no other valid split has fewer K-steps on the critical path (waves of 148 CTAs, each paying
+            # 4 steps' worth of reduction when split)
+            def cost(v):
+                return math.ceil(2 * tiles * v / 148) * (math.ceil(kb / v) + (4 if v > 1 else 0))
+            for v in range(2, 9):
+                if (v - 1) * math.ceil(kb / v) < kb and v <= kb:
+                    assert cost(p["splits"]) <= cost(v), (M, N, Kd, p, v)
+    assert K.gemm_pair_plan(256, 6144, 4096)["splits"] == 3     # Qwen3-8B QKV, 256 tokens: 144 CTAs, one wave
+    assert K.gemm_pair_plan(256, 24576, 4096)["splits"] == 3    # gate-up: 4 waves x (22 + 4) steps beat 2 x 64
+    assert K.gemm_pair_plan(256, 151936, 4096)["splits"] == 1   # LM head: 9 waves unsplit
     assert K.gemm_pair_plan(256, 6144, 4096, splits=5)["splits"] == 5
 
 

@@ -378,3 +378,16 @@ def test_decode_pipeline_gives_the_step_at_a_time_outputs(make_seq, make_config,
     piped = _engine_outputs(make_config, make_seq, True, num_blocks, arrivals)
     assert piped == sync
     assert any(c and c[-1] == 3 for _, c in sync)  # some sequence ended on its end-of-sequence token
+
+
+def test_shared_prefix_workload_shape():
+    """The prefill-heavy benchmark's prompts: one shared 2048-token prefix,
+    unique suffixes of U[512, 6144] tokens, ids in [0, 10000], reproducible."""
+    from kavor_b200.bench_prefix import workload
+
+    prompts = workload(64, 2048, 512, 6144)
+    assert len(prompts) == 64 and prompts == workload(64, 2048, 512, 6144)
+    prefix = prompts[0][:2048]
+    assert all(p[:2048] == prefix and 512 <= len(p) - 2048 <= 6144 for p in prompts)
+    assert all(0 <= t <= 10000 for p in prompts for t in p)
+    assert len({tuple(p[2048:2060]) for p in prompts}) == 64

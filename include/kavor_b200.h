@@ -232,9 +232,16 @@ int kvb_gemm_plan(int M, int N, int K, int splits, int gated, int* plan);
  * operand rules as kvb_gemm_bf16; no workspace. */
 int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N,
                        int K, int splits, void* stream);
-/* The pair GEMM's plan for this shape (host only): plan[0] token tile,
- * plan[1] K splits, plan[2] tiles, plan[3] CTAs. */
-int kvb_gemm_pair_plan(int M, int N, int K, int splits, int* plan);
+/* Gate-up projection fused with SiluAndMul on CTA pairs: w is the [2 * inter,
+ * K] merged weight with rows [gate | up]; the even CTA of each pair holds 128
+ * gate rows, the odd CTA the up rows of the same features, and
+ * y[M, inter] = bf16(silu(bf16(x w_gate^T)) * bf16(x w_up^T)). No K split. */
+int kvb_gemm_pair_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
+                            int inter, int K, void* stream);
+/* The pair GEMM's plan for this shape (host only; gated: N = inter, the
+ * fused SiLU form): plan[0] token tile, plan[1] K splits, plan[2] tiles,
+ * plan[3] CTAs. */
+int kvb_gemm_pair_plan(int M, int N, int K, int splits, int gated, int* plan);
 
 /* Process-wide tuning of kvb_gemm_bf16 / kvb_gemm_silu_bf16 (no reference
  * counterpart): the producer asks L2 for the weight K-steps `ksteps` ahead of

@@ -302,10 +302,10 @@ def gemm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
     return out
 
 
-def gemm_pair_plan(M: int, N: int, K: int, splits: int = 0) -> dict:
+def gemm_pair_plan(M: int, N: int, K: int, splits: int = 0, gated: bool = False) -> dict:
     """Tiling of the CTA-pair GEMM for this shape (token tile, K splits, tiles, CTAs)."""
     out = (ctypes.c_int * 4)()
-    _lib.call("kvb_gemm_pair_plan", M, N, K, splits, out)
+    _lib.call("kvb_gemm_pair_plan", M, N, K, splits, int(gated), out)
     return {"mt": out[0], "splits": out[1], "tiles": out[2], "ctas": out[3]}
 
 
@@ -321,6 +321,22 @@ def gemm_pair(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = 
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
     _lib.call("kvb_gemm_pair_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
               out.stride(0), M, N, K, splits, _stream())
+    return out
+
+
+def gemm_pair_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(x @ w_gate^T) * (x @ w_up^T) for the merged [gate | up] weight on CTA pairs."""
+    _cuda(x, "x", _BF16)
+    _cuda(weight, "weight", _BF16)
+    _req(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1] and weight.shape[0] % 2 == 0,
+         "gemm_pair_silu: x [M, K], weight [2*I, K]")
+    _req(x.stride(1) == 1 and weight.stride(1) == 1, "gemm_pair_silu: rows must be contiguous")
+    M, K = x.shape
+    inter = weight.shape[0] // 2
+    if out is None:
+        out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
+    _lib.call("kvb_gemm_pair_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+              out.data_ptr(), out.stride(0), M, inter, K, _stream())
     return out
 
 

@@ -51,6 +51,7 @@ struct PairArgs {
   int gmax;         // most 8-feature groups a split rank owns: ceil(16 / splits)
   uint32_t idesc;
   int vec_out;      // y rows are 16-byte aligned
+  int up_row0;      // gated: first weight row of the up half (= the output width I)
 };
 
 template <int MT>
@@ -63,6 +64,7 @@ struct PairCfg {
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kTmemCols = MT < 32 ? 32 : MT;    // one fp32 column per token (MT a power of two)
   static constexpr int kPitch = MT + 4;                  // fp32 row pitch of the landing buffer
+  static constexpr int kUpPitch = MT + 8;                // bf16 row pitch of the gated form's up rows
   static constexpr int kSmem = kStages * kStageBytes + 1024;
   static_assert(MT == 64 || MT == 128 || MT == 256, "token tile");
 };
@@ -75,7 +77,14 @@ constexpr bool pair_landing_fits(int splits) {
          (int64_t)PairCfg<MT>::kStages * PairCfg<MT>::kStageBytes;
 }
 
-template <int MT>
+// G (gated, splits = 1): a pair tile is 128 output features; the even CTA
+// holds the gate rows [n0, n0 + 128) and the odd CTA the up rows
+// [I + n0, I + n0 + 128) of the [gate | up] weight (linear.py:76-93 layout),
+// so one pair MMA computes both halves; the odd CTA hands its up values
+// (rounded to bf16, as the reference rounds the projection) to the even CTA
+// through distributed shared memory, which writes bf16(silu(bf16(g)) * u)
+// (activation.py:8-11).
+template <int MT, bool G>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                      const __grid_constant__ PairArgs a) {
@@ -97,7 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_tile = tile % a.m_tiles, n_tile = tile / a.m_tiles;
   const int kb0 = split * a.kb_per_split;
   const int nkb = max(0, min(kb0 + a.kb_per_split, a.kb_total) - kb0);
-  const int n0 = n_tile * 2 * kSlab + member * kSlab;   // this CTA's weight rows = its rows of D
+  // this CTA's weight rows = its rows of D
+  const int n0 = G ? n_tile * kSlab + member * a.up_row0 : n_tile * 2 * kSlab + member * kSlab;
   const int mload = m_tile * MT + member * C::kHalf;    // token rows this CTA stages
   const uint16_t pair_mask = (uint16_t)(3u << (rank & ~1u));
 
@@ -171,6 +181,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after();
   }
 
+  if constexpr (G) {
+    // the odd CTA's up rows, rounded to bf16, land in the even CTA's (free) ring
+    __syncwarp();
+    tc::cluster_sync_all();
+    const int q = warp & 3;  // the TMEM lane quarter this warp may read
+    const int f = q * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    if (warp >= kEpiWarp0 && !dead && member == 1) {
+      const uint32_t dst = tc::map_to_rank(smem_u32(smem) + (uint32_t)(f * C::kUpPitch * 2), rank & ~1u);
+#pragma unroll 1
+      for (int c = 0; c < MT; c += 32) {
+        float v[32];
+        tc::tmem_ld32(trow + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) w4[h] = pack_bf16(v[j + 2 * h], v[j + 2 * h + 1]);
+          tc::st_cluster_v4(dst + (uint32_t)(c + j) * 2, __uint_as_float(w4[0]), __uint_as_float(w4[1]),
+                            __uint_as_float(w4[2]), __uint_as_float(w4[3]));
+        }
+      }
+    }
+    tc::fence_before();
+    __syncwarp();
+    tc::cluster_sync_all();
+    if (warp >= kEpiWarp0 && !dead && member == 0) {
+      const bf16* up = reinterpret_cast<const bf16*>(smem) + f * C::kUpPitch;
+      const int n = n0 + f, m0 = m_tile * MT;
+      const bool in_range = n < a.up_row0;  // the last tile may reach past the I output features
+#pragma unroll 1
+      for (int c = 0; c < MT; c += 32) {
+        float v[32];
+        tc::tmem_ld32(trow + c, v);  // the whole warp, converged
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c + j;
+          if (in_range && m < a.M) {
+            const float g = bf16_round(v[j]);
+            a.y[(int64_t)m * a.ldy + n] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * __bfloat162float(up[c + j]));
+          }
+        }
+      }
+    }
+  } else {
   // part 2: every CTA of the cluster has seen its accumulator complete, so every
   // stage ring is free; push the fp32 rows to the CTAs (same pair position)
   // that own each 8-feature group
@@ -235,6 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  }  // not gated
+
   // TMEM reads are done in both CTAs of the pair before either frees the pair's allocation
   tc::fence_before();
   tc::cluster_sync_all();
@@ -281,10 +338,11 @@ bool landing_fits(int mt, int splits) {
 // (reduced until valid).
 constexpr int kReduceSteps = 4;
 
-PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
+// gated: N is the output width I, a tile is 128 features (gate and up rows), splits = 1.
+PairPlan make_pair_plan(int M, int N, int K, int splits_req, bool gated = false) {
   PairPlan p;
   p.mt = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
-  p.n_tiles = (N + 2 * kSlab - 1) / (2 * kSlab);
+  p.n_tiles = gated ? (N + kSlab - 1) / kSlab : (N + 2 * kSlab - 1) / (2 * kSlab);
   p.m_tiles = (M + p.mt - 1) / p.mt;
   p.kb_total = (K + kBK - 1) / kBK;
   const int tiles = p.n_tiles * p.m_tiles;
@@ -294,7 +352,9 @@ PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
     return (v - 1) * per < p.kb_total && landing_fits(p.mt, v);
   };
   int s = 1;
-  if (splits_req > 0) {
+  if (gated) {
+    s = 1;
+  } else if (splits_req > 0) {
     s = splits_req > kMaxSplits ? kMaxSplits : splits_req;
     while (s > 1 && !valid(s)) --s;
   } else {
@@ -318,15 +378,18 @@ PairPlan make_pair_plan(int M, int N, int K, int splits_req) {
 
 std::atomic<unsigned long long> g_attr_done{0};
 
-template <int MT>
+template <int MT, bool G>
 int launch_pair(const CUtensorMap& wmap, const CUtensorMap& xmap, const PairArgs& a, int ctas, cudaStream_t stream) {
   using C = PairCfg<MT>;
   int dev = 0;
   cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << ((dev & 15) * 3 + (MT == 64 ? 0 : (MT == 128 ? 1 : 2)));
-  if (!(g_attr_done.load() & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_pair_kernel<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  // kernel attributes are set once per device (up to 8 cached; others every call)
+  const unsigned long long bit =
+      dev >= 0 && dev < 8 ? 1ull << (dev * 6 + (G ? 3 : 0) + (MT == 64 ? 0 : (MT == 128 ? 1 : 2))) : 0;
+  if (!bit || !(g_attr_done.load() & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<MT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_pair_kernel<MT, G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_status(e, "gemm pair kernel attributes");
     g_attr_done.fetch_or(bit);
   }
@@ -344,36 +407,21 @@ int launch_pair(const CUtensorMap& wmap, const CUtensorMap& xmap, const PairArgs
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<MT>, wmap, xmap, a), "kvb_gemm_pair_bf16 launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<MT, G>, wmap, xmap, a), "kvb_gemm_pair launch");
 }
 
-}  // namespace
-}  // namespace kvb
-
-using namespace kvb;
-
-extern "C" int kvb_gemm_pair_plan(int M, int N, int K, int splits, int* plan) {
-  if (!plan || M <= 0 || N <= 0 || K <= 0 || splits < 0 || splits > kMaxSplits)
-    return set_error(kInvalid, "kvb_gemm_pair_plan: bad sizes");
-  const PairPlan p = make_pair_plan(M, N, K, splits);
-  plan[0] = p.mt;
-  plan[1] = p.splits;
-  plan[2] = p.n_tiles * p.m_tiles;
-  plan[3] = p.ctas;
-  return kOk;
-}
-
-extern "C" int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
-                                  int N, int K, int splits, void* stream) {
-  if (M < 0 || N <= 0 || K <= 0 || splits < 0 || splits > kMaxSplits || ldx < K || ldw < K || ldy < N)
-    return set_error(kInvalid, "kvb_gemm_pair_bf16: bad sizes or leading dimensions");
+// y[M, n_out] = x w^T (gated: w = [gate | up] with n_out rows each, y = silu(x w_gate^T) * (x w_up^T)).
+int run_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int n_out, int K,
+             int splits, void* stream, bool gated, const char* name) {
+  if (M < 0 || n_out <= 0 || K <= 0 || splits < 0 || splits > kMaxSplits || ldx < K || ldw < K || ldy < n_out)
+    return set_error(kInvalid, "%s: bad sizes or leading dimensions", name);
   if (M == 0) return kOk;
-  if (!x || !w || !y) return set_error(kInvalid, "kvb_gemm_pair_bf16: NULL pointer");
+  if (!x || !w || !y) return set_error(kInvalid, "%s: NULL pointer", name);
   if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ldx % 8 || ldw % 8 || K % 8)
-    return set_error(kInvalid, "kvb_gemm_pair_bf16: x/w rows must be 16-byte aligned (K, ldx, ldw multiples of 8)");
-  const PairPlan p = make_pair_plan(M, N, K, splits);
+    return set_error(kInvalid, "%s: x/w rows must be 16-byte aligned (K, ldx, ldw multiples of 8)", name);
+  const PairPlan p = make_pair_plan(M, n_out, K, splits, gated);
   CUtensorMap wmap, xmap;
-  int rc = encode_rows(&wmap, w, N, K, ldw, kSlab);
+  int rc = encode_rows(&wmap, w, (int64_t)n_out * (gated ? 2 : 1), K, ldw, kSlab);
   if (rc) return rc;
   rc = encode_rows(&xmap, x, M, K, ldx, p.mt / 2);
   if (rc) return rc;
@@ -381,7 +429,7 @@ extern "C" int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int
   a.y = (bf16*)y;
   a.ldy = ldy;
   a.M = M;
-  a.N = N;
+  a.N = n_out;
   a.n_tiles = p.n_tiles;
   a.m_tiles = p.m_tiles;
   a.splits = p.splits;
@@ -391,10 +439,44 @@ extern "C" int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int
   // f32 D (bit 4), bf16 A and B (bits 7, 10), both K-major; N = MT (bits 17..22, N >> 3), M = 256 (bits 24..28, M >> 4)
   a.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.mt >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
   a.vec_out = ((uintptr_t)y & 15) == 0 && ldy % 8 == 0;
+  a.up_row0 = n_out;
   cudaStream_t st = (cudaStream_t)stream;
-  switch (p.mt) {
-    case 64: return launch_pair<64>(wmap, xmap, a, p.ctas, st);
-    case 128: return launch_pair<128>(wmap, xmap, a, p.ctas, st);
-    default: return launch_pair<256>(wmap, xmap, a, p.ctas, st);
+  if (gated) {
+    switch (p.mt) {
+      case 64: return launch_pair<64, true>(wmap, xmap, a, p.ctas, st);
+      case 128: return launch_pair<128, true>(wmap, xmap, a, p.ctas, st);
+      default: return launch_pair<256, true>(wmap, xmap, a, p.ctas, st);
+    }
   }
+  switch (p.mt) {
+    case 64: return launch_pair<64, false>(wmap, xmap, a, p.ctas, st);
+    case 128: return launch_pair<128, false>(wmap, xmap, a, p.ctas, st);
+    default: return launch_pair<256, false>(wmap, xmap, a, p.ctas, st);
+  }
+}
+
+}  // namespace
+}  // namespace kvb
+
+using namespace kvb;
+
+extern "C" int kvb_gemm_pair_plan(int M, int N, int K, int splits, int gated, int* plan) {
+  if (!plan || M <= 0 || N <= 0 || K <= 0 || splits < 0 || splits > kMaxSplits)
+    return set_error(kInvalid, "kvb_gemm_pair_plan: bad sizes");
+  const PairPlan p = make_pair_plan(M, N, K, splits, gated != 0);
+  plan[0] = p.mt;
+  plan[1] = p.splits;
+  plan[2] = p.n_tiles * p.m_tiles;
+  plan[3] = p.ctas;
+  return kOk;
+}
+
+extern "C" int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
+                                  int N, int K, int splits, void* stream) {
+  return run_pair(x, ldx, w, ldw, y, ldy, M, N, K, splits, stream, false, "kvb_gemm_pair_bf16");
+}
+
+extern "C" int kvb_gemm_pair_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                                       int M, int inter, int K, void* stream) {
+  return run_pair(x, ldx, w, ldw, y, ldy, M, inter, K, 1, stream, true, "kvb_gemm_pair_silu_bf16");
 }

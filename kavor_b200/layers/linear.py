@@ -9,7 +9,8 @@ package. Which GEMM runs is a process-wide choice (``set_gemm_backend``):
 "cublas" (torch's F.linear, the reference's own GEMM; the default),
 "tcgen05" (this package's kernel, kvb_gemm_bf16, with the gate-up projection
 and SiluAndMul fused into kvb_gemm_silu_bf16 by the MLP) or "tcgen05_pair"
-(the CTA-pair kernel, kvb_gemm_pair_bf16, for every projection).
+(the CTA-pair kernel, kvb_gemm_pair_bf16, and its fused gate-up + SiLU form
+kvb_gemm_pair_silu_bf16).
 """
 from __future__ import annotations
 

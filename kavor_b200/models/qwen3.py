@@ -105,8 +105,11 @@ class Qwen3MLP(nn.Module):
         self.act_fn = SiluAndMul()
 
     def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
-        if gemm_backend() == "tcgen05":  # gate-up projection and SiluAndMul in one kernel
+        backend = gemm_backend()
+        if backend == "tcgen05":  # gate-up projection and SiluAndMul in one kernel
             return self.down_proj(K.gemm_silu(x, self.gate_up_proj.weight), reduce=reduce, out=out)
+        if backend == "tcgen05_pair":
+            return self.down_proj(K.gemm_pair_silu(x, self.gate_up_proj.weight), reduce=reduce, out=out)
         return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce, out=out)
 
 

@@ -7,7 +7,8 @@ cuBLAS (torch.matmul) on the same operands.
 (default M 1,64,256; K splits 1,2,4,8,16; L2 prefetch distance 0). Every
 variant runs at every L2 prefetch distance given (kvb_gemm_set_l2_prefetch);
 labels carry a "_pfN" suffix when N > 0. --pair adds the CTA-pair kernel
-(kvb_gemm_pair_bf16): "pair_auto" and "pair_sN" for K splits N <= 8.
+(kvb_gemm_pair_bf16): "pair_auto" and "pair_sN" for K splits N <= 8, and
+"g_pair" (kvb_gemm_pair_silu_bf16) for the gate-up shapes.
 
 Shapes: QKV, O, gate-up, down and LM head of Qwen3-8B at TP=1 and TP=8. Each
 timing is one replay of a CUDA graph of 20 launches (device time, CUDA events),
@@ -105,6 +106,10 @@ def main(argv=None) -> int:
                     err = (out.float() - ref.float()).abs().max().item()
                     t = _timeit(lambda i: K.gemm_pair(x, ws[i % len(ws)], out=out, splits=splits))
                     res[label] = [round(t, 2), round(nbytes / t / 1e3), p["mt"], round(err, 4)]
+                if name.startswith("gate_up"):
+                    og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+                    t = _timeit(lambda i: K.gemm_pair_silu(x, ws[i % len(ws)], out=og))
+                    res["g_pair"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_pair_plan(M, N // 2, Kd, 0, True)["mt"]]
             t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
             res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
             res["device_error_bits"] = _lib.device_error(clear=True)

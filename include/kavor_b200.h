@@ -235,9 +235,10 @@ int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, v
 /* Gate-up projection fused with SiluAndMul on CTA pairs: w is the [2 * inter,
  * K] merged weight with rows [gate | up]; the even CTA of each pair holds 128
  * gate rows, the odd CTA the up rows of the same features, and
- * y[M, inter] = bf16(silu(bf16(x w_gate^T)) * bf16(x w_up^T)). No K split. */
+ * y[M, inter] = bf16(silu(bf16(x w_gate^T)) * bf16(x w_up^T)). K split as
+ * kvb_gemm_pair_bf16 (0 = planned). */
 int kvb_gemm_pair_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
-                            int inter, int K, void* stream);
+                            int inter, int K, int splits, void* stream);
 /* The pair GEMM's plan for this shape (host only; gated: N = inter, the
  * fused SiLU form): plan[0] token tile, plan[1] K splits, plan[2] tiles,
  * plan[3] CTAs. */

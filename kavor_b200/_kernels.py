@@ -324,7 +324,8 @@ def gemm_pair(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = 
     return out
 
 
-def gemm_pair_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def gemm_pair_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+                   splits: int = 0) -> torch.Tensor:
     """silu(x @ w_gate^T) * (x @ w_up^T) for the merged [gate | up] weight on CTA pairs."""
     _cuda(x, "x", _BF16)
     _cuda(weight, "weight", _BF16)
@@ -336,7 +337,7 @@ def gemm_pair_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | No
     if out is None:
         out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
     _lib.call("kvb_gemm_pair_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
-              out.data_ptr(), out.stride(0), M, inter, K, _stream())
+              out.data_ptr(), out.stride(0), M, inter, K, splits, _stream())
     return out
 
 

@@ -43,7 +43,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_gemm_plan": [I, I, I, I, I, POINTER(c_int)],
     "kvb_gemm_set_l2_prefetch": [I],
     "kvb_gemm_pair_bf16": [P, L, P, L, P, L, I, I, I, I, P],
-    "kvb_gemm_pair_silu_bf16": [P, L, P, L, P, L, I, I, I, P],
+    "kvb_gemm_pair_silu_bf16": [P, L, P, L, P, L, I, I, I, I, P],
     "kvb_gemm_pair_plan": [I, I, I, I, I, POINTER(c_int)],
     "kvb_set_pdl": [I],
     "kvb_gemm_silu_workspace_size": [I, I, I, I, POINTER(c_size_t)],

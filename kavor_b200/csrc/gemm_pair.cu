@@ -70,10 +70,12 @@ struct PairCfg {
 };
 
 // Landing buffer (the stage ring) of a K split: per source split, gmax groups
-// of 8 feature rows of MT + 4 floats.
+// of 8 feature rows of MT + 4 floats; the gated form adds the up owner's
+// gmax x 8 bf16 rows of MT + 8.
 template <int MT>
-constexpr bool pair_landing_fits(int splits) {
-  return (int64_t)splits * ((16 + splits - 1) / splits) * 8 * PairCfg<MT>::kPitch * 4 <=
+constexpr bool pair_landing_fits(int splits, bool gated) {
+  const int64_t rows = (int64_t)((16 + splits - 1) / splits) * 8;
+  return splits * rows * PairCfg<MT>::kPitch * 4 + (gated ? rows * PairCfg<MT>::kUpPitch * 2 : 0) <=
          (int64_t)PairCfg<MT>::kStages * PairCfg<MT>::kStageBytes;
 }
 
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after();
   }
 
-  if constexpr (G) {
+  if (G && a.splits == 1) {
     // the odd CTA's up rows, rounded to bf16, land in the even CTA's (free) ring
     __syncwarp();
     tc::cluster_sync_all();
@@ -254,8 +256,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_before();
   __syncwarp();
   tc::cluster_sync_all();
+  if (G) {
+    // gated with a K split: each CTA of split o now owns groups [g0, g0 + ng)
+    // of its member's rows (gate in even CTAs, up in odd); the up owner sums
+    // its parts, rounds them to bf16 and stores them behind the gate owner's
+    // landing area; after the barrier the gate owner writes silu(g) * u
+    const float* rf = reinterpret_cast<const float*>(smem);
+    const int e = threadIdx.x - kEpiWarp0 * 32;
+    const int g0 = split * 16 / Cn, ng = (split + 1) * 16 / Cn - g0;
+    const int groups = ng * MT;
+    const uint32_t up_off = (uint32_t)(Cn * rows_per_src * C::kPitch * 4);
+    if (warp >= kEpiWarp0 && !dead && member == 1) {
+      const uint32_t ub = tc::map_to_rank(red + up_off, rank & ~1u);
+#pragma unroll 1
+      for (int g = e; g < groups; g += 128) {
+        const int ml = g % MT, fg = g / MT;
+        if (m_tile * MT + ml >= a.M) continue;
+#pragma unroll 1
+        for (int j = 0; j < 8; ++j) {
+          float acc = 0.f;
+          for (int s2 = 0; s2 < Cn; ++s2) acc += rf[(s2 * rows_per_src + fg * 8 + j) * C::kPitch + ml];
+          const bf16 h = __float2bfloat16_rn(acc);
+          tc::st_cluster_b16(ub + (uint32_t)(((fg * 8 + j) * C::kUpPitch + ml) * 2),
+                             *reinterpret_cast<const unsigned short*>(&h));
+        }
+      }
+    }
+    tc::fence_before();
+    __syncwarp();
+    tc::cluster_sync_all();
+    if (warp >= kEpiWarp0 && !dead && member == 0) {
+      const bf16* up = reinterpret_cast<const bf16*>(smem + up_off);
+      const int nb = n0 + g0 * 8, m0 = m_tile * MT;
+#pragma unroll 1
+      for (int g = e; g < groups; g += 128) {
+        const int ml = g % MT, fg = g / MT;
+        const int m = m0 + ml;
+        if (m >= a.M) continue;
+        float y8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float acc = 0.f;
+          for (int s2 = 0; s2 < Cn; ++s2) acc += rf[(s2 * rows_per_src + fg * 8 + j) * C::kPitch + ml];
+          const float gt = bf16_round(acc);
+          y8[j] = gt / (1.f + __expf(-gt)) * __bfloat162float(up[(fg * 8 + j) * C::kUpPitch + ml]);
+        }
+        const int n = nb + fg * 8;
+        if (n >= a.up_row0) continue;
+        bf16* yr = a.y + (int64_t)m * a.ldy + n;
+        if (a.vec_out && n + 8 <= a.up_row0) {
+          uint4 pk;
+          __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h2[j] = __floats2bfloat162_rn(y8[2 * j], y8[2 * j + 1]);
+          *reinterpret_cast<uint4*>(yr) = pk;
+        } else {
+          for (int j = 0; j < 8 && n + j < a.up_row0; ++j) yr[j] = __float2bfloat16_rn(y8[j]);
+        }
+      }
+    }
+  }
   // part 3: this CTA owns feature groups [g0, g0 + ng) of its 128 rows
-  if (warp >= kEpiWarp0 && !dead) {
+  if (!G && warp >= kEpiWarp0 && !dead) {
     const float* rf = reinterpret_cast<const float*>(smem);
     const int e = threadIdx.x - kEpiWarp0 * 32;
     const int g0 = split * 16 / Cn, ng = (split + 1) * 16 / Cn - g0;
@@ -320,11 +382,11 @@ struct PairPlan {
   int mt, n_tiles, m_tiles, splits, kb_total, kb_per_split, ctas;
 };
 
-bool landing_fits(int mt, int splits) {
+bool landing_fits(int mt, int splits, bool gated) {
   switch (mt) {
-    case 64: return pair_landing_fits<64>(splits);
-    case 128: return pair_landing_fits<128>(splits);
-    default: return pair_landing_fits<256>(splits);
+    case 64: return pair_landing_fits<64>(splits, gated);
+    case 128: return pair_landing_fits<128>(splits, gated);
+    default: return pair_landing_fits<256>(splits, gated);
   }
 }
 
@@ -338,7 +400,7 @@ bool landing_fits(int mt, int splits) {
 // (reduced until valid).
 constexpr int kReduceSteps = 4;
 
-// gated: N is the output width I, a tile is 128 features (gate and up rows), splits = 1.
+// gated: N is the output width I, a tile is 128 features (gate and up rows).
 PairPlan make_pair_plan(int M, int N, int K, int splits_req, bool gated = false) {
   PairPlan p;
   p.mt = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
@@ -349,12 +411,10 @@ PairPlan make_pair_plan(int M, int N, int K, int splits_req, bool gated = false)
   auto valid = [&](int v) {
     if (v > p.kb_total) return false;
     const int per = (p.kb_total + v - 1) / v;
-    return (v - 1) * per < p.kb_total && landing_fits(p.mt, v);
+    return (v - 1) * per < p.kb_total && landing_fits(p.mt, v, gated);
   };
   int s = 1;
-  if (gated) {
-    s = 1;
-  } else if (splits_req > 0) {
+  if (splits_req > 0) {
     s = splits_req > kMaxSplits ? kMaxSplits : splits_req;
     while (s > 1 && !valid(s)) --s;
   } else {
@@ -477,6 +537,6 @@ extern "C" int kvb_gemm_pair_bf16(const void* x, int64_t ldx, const void* w, int
 }
 
 extern "C" int kvb_gemm_pair_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
-                                       int M, int inter, int K, void* stream) {
-  return run_pair(x, ldx, w, ldw, y, ldy, M, inter, K, 1, stream, true, "kvb_gemm_pair_silu_bf16");
+                                       int M, int inter, int K, int splits, void* stream) {
+  return run_pair(x, ldx, w, ldw, y, ldy, M, inter, K, splits, stream, true, "kvb_gemm_pair_silu_bf16");
 }

@@ -33,6 +33,10 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
                : "memory");
 }
 
+__device__ __forceinline__ void st_cluster_b16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared::cluster.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA
 // 2-D tiled load into this CTA's shared memory whose completion (bytes) is
 // counted on `bar`, a shared::cluster address that may be the barrier of the

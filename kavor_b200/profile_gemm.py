@@ -109,7 +109,8 @@ def main(argv=None) -> int:
                 if name.startswith("gate_up"):
                     og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
                     t = _timeit(lambda i: K.gemm_pair_silu(x, ws[i % len(ws)], out=og))
-                    res["g_pair"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_pair_plan(M, N // 2, Kd, 0, True)["mt"]]
+                    res["g_pair"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_pair_plan(M, N // 2, Kd, 0, True)["mt"],
+                                     K.gemm_pair_plan(M, N // 2, Kd, 0, True)["splits"]]
             t = _timeit(lambda i: torch.matmul(x, ws[i % len(ws)].t(), out=out))
             res["cublas"] = [round(t, 2), round(nbytes / t / 1e3)]
             res["device_error_bits"] = _lib.device_error(clear=True)

@@ -71,7 +71,7 @@ CASES = [
     ("kvb_gemm_pair_bf16", (ODD, 64, FAKE, 64, FAKE, 64, 16, 64, 64, 0, NULL), INVALID, "aligned"),
     ("kvb_gemm_pair_plan", (0, 64, 64, 0, 0, ctypes.cast(ctypes.create_string_buffer(16), ctypes.POINTER(ctypes.c_int))),
      INVALID, "bad sizes"),
-    ("kvb_gemm_pair_silu_bf16", (FAKE, 32, FAKE, 64, FAKE, 64, 16, 64, 64, NULL), INVALID, "bad sizes"),  # ldx < K
+    ("kvb_gemm_pair_silu_bf16", (FAKE, 32, FAKE, 64, FAKE, 64, 16, 64, 64, 0, NULL), INVALID, "bad sizes"),  # ldx < K
 ]
 
 

@@ -59,15 +59,16 @@ def test_gemm_pair_split_is_deterministic():
     torch.testing.assert_close(a.float(), K_.gemm_pair(x, w, splits=1).float(), atol=1e-2, rtol=1e-2)
 
 
-@pytest.mark.parametrize("M,inter,K", [(1, 1536, 4096), (64, 3072, 1024), (100, 1000, 4096), (256, 12288, 4096),
-                                       (300, 1536, 4096)])
-def test_gemm_pair_silu_matches_the_rounded_reference(M, inter, K):
+@pytest.mark.parametrize("M,inter,K,splits", [(1, 1536, 4096, 0), (64, 3072, 1024, 1), (100, 1000, 4096, 0),
+                                              (256, 12288, 4096, 1), (256, 12288, 4096, 3), (300, 1536, 4096, 0),
+                                              (256, 1536, 4096, 6), (33, 768, 4096, 5)])
+def test_gemm_pair_silu_matches_the_rounded_reference(M, inter, K, splits):
     """bf16(silu(bf16(x w_gate^T)) * bf16(x w_up^T)), the reference's rounding points."""
     from kavor_b200 import _kernels as K_
 
     x, w = _inputs(M, 2 * inter, K, seed=7)
     out = torch.full((M, inter), float("nan"), dtype=torch.bfloat16, device=DEV)
-    K_.gemm_pair_silu(x, w, out=out)
+    K_.gemm_pair_silu(x, w, out=out, splits=splits)
     ref32 = x.float() @ w.float().t()
     g, u = ref32[:, :inter].to(torch.bfloat16).float(), ref32[:, inter:].to(torch.bfloat16).float()
     torch.testing.assert_close(out.float(), F.silu(g) * u, atol=2e-2, rtol=2e-2)

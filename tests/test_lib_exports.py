@@ -142,11 +142,12 @@ def test_gemm_pair_plans(lib):
     assert K.gemm_pair_plan(256, 24576, 4096)["splits"] == 3    # gate-up: 4 waves x (22 + 4) steps beat 2 x 64
     assert K.gemm_pair_plan(256, 151936, 4096)["splits"] == 1   # LM head: 9 waves unsplit
     assert K.gemm_pair_plan(256, 6144, 4096, splits=5)["splits"] == 5
-    for M, inter in ((1, 1536), (100, 3072), (256, 12288), (300, 1000)):  # gated: 128-feature tiles, no split
+    for M, inter in ((1, 1536), (100, 3072), (256, 12288), (300, 1000)):  # gated: 128-feature tiles
         mt = 64 if M <= 64 else (128 if M <= 128 else 256)
         p = K.gemm_pair_plan(M, inter, 4096, gated=True)
-        assert p["splits"] == 1 and p["tiles"] == math.ceil(inter / 128) * math.ceil(M / mt)
-        assert p["ctas"] == 2 * p["tiles"] and p["mt"] == mt
+        assert p["tiles"] == math.ceil(inter / 128) * math.ceil(M / mt) and p["mt"] == mt
+        assert p["ctas"] == 2 * p["tiles"] * p["splits"]
+    assert K.gemm_pair_plan(256, 1536, 4096, gated=True)["splits"] == 6   # TP=8 gate-up: 12 tiles x 6 x 2 = 144 CTAs
 
 
 def test_allreduce_plan_matches_the_documented_choice(lib):

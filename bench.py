@@ -62,6 +62,8 @@ def parse_args(argv=None):
     ap.add_argument("--gemm-l2-prefetch", type=int, default=0,
                     help="tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads")
     ap.add_argument("--pdl", action="store_true", help="programmatic dependent launch of the package's kernels")
+    ap.add_argument("--no-probes", action="store_true",
+                    help="skip the one-GPU probes of the package's GEMM in place of cuBLAS")
     ap.add_argument("--e2e-pipelined", action="store_true",
                     help="e2e through ModelRunner.run_async with one step in flight (host work overlaps the GPU)")
     return ap.parse_args(argv)
@@ -454,6 +456,12 @@ def run_ours(args) -> int:
     e2e_pipelined = None
     if world == 1 and not args.no_e2e and not args.e2e_pipelined:
         e2e_pipelined = _e2e_pipelined_probe(runner, seqs, bm, args)
+    # the decode step with the package's GEMM in place of cuBLAS (re-captured graphs; same guard)
+    gemm_probes = None
+    if world == 1 and args.gemm == "cublas" and not args.no_probes:
+        graph = None  # the probes re-capture the decode graph
+        gemm_probes = {f"{backend}_l2pf{pf}": _gemm_backend_probe(runner, seqs, B, args, backend, pf)
+                       for backend, pf in (("tcgen05", 0), ("tcgen05", 8))}
 
     if rank == 0:
         line = {
@@ -467,6 +475,8 @@ def run_ours(args) -> int:
         }
         if e2e_pipelined is not None:
             line["e2e_pipelined"] = e2e_pipelined
+        if gemm_probes is not None:
+            line["gemm_backend_probes"] = gemm_probes
         print(json.dumps(line), flush=True)
     # graphs hold NCCL work: every reference must be gone before the group is destroyed
     del graph
@@ -476,10 +486,52 @@ def run_ours(args) -> int:
         barrier()
         dist.destroy_process_group()
     except Exception:
-        if e2e_pipelined is None or "error" not in e2e_pipelined:
+        probes = [e2e_pipelined] + list((gemm_probes or {}).values())
+        if not any(p is not None and "error" in p for p in probes):
             raise
-        print(f"teardown after the failed pipelined probe: {sys.exc_info()[1]}", file=sys.stderr, flush=True)
+        print(f"teardown after a failed probe: {sys.exc_info()[1]}", file=sys.stderr, flush=True)
     return 0
+
+
+def _gemm_backend_probe(runner, seqs, B, args, backend: str, l2_prefetch: int) -> dict:
+    """Device time of the decode step with every projection on the package's
+    GEMM (Config.gemm_backend) instead of cuBLAS: the decode graph re-captured,
+    the same resident batch, `steps` replays after `warmup`."""
+    from kavor_b200 import _kernels as K
+    from kavor_b200 import _lib
+    from kavor_b200.layers.linear import set_gemm_backend
+
+    try:
+        set_gemm_backend(backend)
+        K.gemm_set_l2_prefetch(l2_prefetch)
+        runner.graphs.clear()
+        runner.graph_pool = None
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        runner.capture_cudagraph()
+        runner.run(seqs, False)  # the re-captured graph's static inputs
+        graph = runner.graphs[next(b for b in runner.graph_bs if b >= B)]
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3
+        return {"value": B * args.steps / t, "unit": "tok/s", "ms_per_step": t / args.steps * 1e3,
+                "gemm_backend": backend, "l2_prefetch_ksteps": l2_prefetch,
+                "device_error_bits": _lib.device_error(clear=True)}
+    except Exception as exc:  # the probe of an option that is off by default must not cost the main line
+        return {"error": f"{type(exc).__name__}: {exc}"[:400]}
+    finally:
+        set_gemm_backend("cublas")
+        try:
+            K.gemm_set_l2_prefetch(0)
+        except Exception:
+            pass
 
 
 def _e2e_pipelined_probe(runner, seqs, bm, args) -> dict:

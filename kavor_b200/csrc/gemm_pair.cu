@@ -67,6 +67,8 @@ struct PairCfg {
   static constexpr int kUpPitch = MT + 8;                // bf16 row pitch of the gated form's up rows
   static constexpr int kSmem = kStages * kStageBytes + 1024;
   static_assert(MT == 64 || MT == 128 || MT == 256, "token tile");
+  static_assert(kSmem <= 227 * 1024, "dynamic shared memory of one CTA");
+  static_assert(kTmemCols <= 512, "TMEM columns of one SM");
 };
 
 // Landing buffer (the stage ring) of a K split: per source split, gmax groups

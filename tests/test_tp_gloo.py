@@ -154,6 +154,62 @@ def test_mailbox_carries_calls_to_workers():
         shm.unlink()
 
 
+def _slow_mailbox_worker(name, event, conn, delay):
+    import time
+    from multiprocessing.shared_memory import SharedMemory
+
+    from kavor_b200.engine.model_runner import ModelRunner
+
+    shm = SharedMemory(name=name)
+    calls = []
+    runner = SimpleNamespace(shm=shm, event=event, world_size=WORLD, rank=1)
+    while True:
+        time.sleep(delay)  # a worker still busy with its previous step
+        method, args = ModelRunner.read_shm(runner)
+        calls.append((method, args))
+        if method == "exit":
+            break
+    conn.send(calls)
+    shm.close()
+
+
+def test_mailbox_writes_wait_for_a_slow_worker():
+    """Calls that return before their step completes (run_async) can reach
+    the mailbox again before a worker has read the last message: the write
+    waits until every worker has taken it, so no message is overwritten."""
+    import multiprocessing as mp
+    from multiprocessing.shared_memory import SharedMemory
+
+    from kavor_b200.engine.model_runner import SHM_BYTES, ModelRunner
+
+    ctx = mp.get_context("spawn")
+    name = f"kvb_slow_{os.getpid()}"
+    shm = SharedMemory(name=name, create=True, size=SHM_BYTES)
+    try:
+        ev = ctx.Event()
+        recv, send = ctx.Pipe(duplex=False)
+        p = ctx.Process(target=_slow_mailbox_worker, args=(name, ev, send, 0.3))
+        p.start()
+        runner = SimpleNamespace(shm=shm, event=[ev], world_size=WORLD, rank=0)
+        try:
+            for i in range(4):  # back to back, no waiting on the caller's side
+                ModelRunner.write_shm(runner, "run_async", [f"step{i}"], i > 0)
+            ModelRunner.write_shm(runner, "exit")
+            assert recv.poll(60), "the worker never saw its exit message"
+            calls = recv.recv()
+            p.join(timeout=60)
+            assert p.exitcode == 0
+        finally:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+        assert calls == [("run_async", [["step0"], False]), ("run_async", [["step1"], True]),
+                         ("run_async", [["step2"], True]), ("run_async", [["step3"], True]), ("exit", [])]
+    finally:
+        shm.close()
+        shm.unlink()
+
+
 def test_allreduce_buffer_schedule_never_reuses_consecutively():
     """The decode step's 2L+1 fused all-reduces alternate data buffers so two
     consecutive reductions (also across steps) never share one."""

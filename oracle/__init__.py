@@ -6,8 +6,9 @@ path, so the sm_100a kernels of ``kavor_b200`` can be checked against it:
 * ``oracle.ops``   — per-kernel restatements (fp32 torch on CPU for the
   floating-point ops, plain index arithmetic for the KV write / metadata),
   each citing the reference file:line it follows;
-* ``oracle.model`` — the Qwen3 decoder layer / model forward composed from
-  ``oracle.ops`` with the reference's residual wiring (qwen3.py:149-186);
+* ``oracle.model`` — the Qwen3 (and Mistral, ERNIE 4.5) decoder layer / model
+  forward composed from ``oracle.ops`` with the reference's residual wiring
+  (qwen3.py:149-186);
 * ``oracle.host``  — the reference's host-side batch metadata algorithm
   (model_runner.py:385-473) as straight Python loops.
 
@@ -19,7 +20,10 @@ third-party kernels the reference calls (flash-attn 2.8.3.post2 for
 attention, NCCL for the all-reduce) are not in the reference tree and cannot
 run on a CPU: attention is restated from flash-attn's documented semantics
 (causal bottom-right alignment, fp32 softmax, scale head_dim**-0.5, GQA
-head mapping) and is parity-unpinned at that boundary.
+head mapping). On the CPU that boundary is unpinned; on the GPU the same
+flash-attn wheel runs beside the kernels on identical inputs
+(tests/test_flash_attn_parity_gpu.py), which the kernels also match against
+this oracle.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
 ``bench.py`` may import this package. The product (``kavor_b200``) never does.

@@ -64,9 +64,13 @@ SIGNATURES: dict[str, list] = {
 _lib: ctypes.CDLL | None = None
 
 # Entry points that only query or report (everything else launches kernels).
-_QUERIES = {"kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
-            "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch", "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach", "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
-            "kvb_comm_data_buffer", "kvb_comm_destroy"}
+_QUERIES = {
+    "kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
+    "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch",
+    "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach",
+    "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
+    "kvb_comm_data_buffer", "kvb_comm_destroy",
+}
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.
 CALLS: dict[str, int] = {}

@@ -58,7 +58,8 @@ def main(argv=None) -> int:
     total = sum(sp.max_tokens for sp in params)
     generated = sum(len(o["token_ids"]) for o in out)
     print(json.dumps({"workload": f"offline generate, {a.model}, {a.num_seqs} seqs, prompt/output U[100,1024]",
-                      "tp": a.tp, "async_decode": a.async_decode, "gemm": a.gemm, "pdl": a.pdl, "total_tokens": total, "generated_tokens": generated, "seconds": dt,
+                      "tp": a.tp, "async_decode": a.async_decode, "gemm": a.gemm, "pdl": a.pdl,
+                      "total_tokens": total, "generated_tokens": generated, "seconds": dt,
                       "tok_s": total / dt, "reference_published_tok_s": REFERENCE_PUBLISHED_TOK_S,
                       "reference_hardware": "RTX 4070 Laptop 8 GB (README.md:44-55)"}), flush=True)
     return 0 if generated == total else 1

@@ -40,6 +40,13 @@ def hf_config(shape: dict, **over):
 FAMILIES = ("mistral", "ernie4_5")
 
 
+def prefix_cache_prompts() -> tuple[list[int], list[int]]:
+    """Prompt A (300 tokens) and the 40 new tokens that follow A's first 256
+    (one full block) in prompt B."""
+    g = torch.Generator().manual_seed(21)
+    return (torch.randint(3, 4000, (300,), generator=g).tolist(), torch.randint(3, 4000, (40,), generator=g).tolist())
+
+
 def family_config(family: str):
     from transformers import Ernie4_5Config, MistralConfig
 
@@ -229,3 +236,63 @@ def check_greedy_step(logits: torch.Tensor, step: dict, min_cos: float = 0.999, 
             assert mine == ref, (b, mine, ref, margin)
             checked += 1
     return checked
+
+
+def replay_prefix_cache(gold: dict, run_step):
+    """Teacher-forced replay of the prefix-cache fixture (make_golden.golden_prefix_cache):
+    prefill A; prefill B's new tokens over the cached block 0 (cu_seqlens_k >
+    cu_seqlens_q, block_tables given); then 4 decode steps of A and B. Yields
+    (logits, step record); batches as in ``replay`` plus cu_seqlens_k and,
+    for B's prefill, block_tables."""
+    a, b_new, tables = gold["a_prompt"], gold["b_new"], gold["tables"]
+    b = a[:256] + b_new
+    i32 = torch.int32
+
+    def slot(row, pos):
+        return tables[row][pos // 256] * 256 + pos % 256
+
+    n = len(a)
+    batches = [dict(is_prefill=True, input_ids=torch.tensor(a), positions=torch.arange(n),
+                    cu_seqlens=torch.tensor([0, n], dtype=i32), cu_seqlens_k=torch.tensor([0, n], dtype=i32),
+                    slot_mapping=torch.tensor([slot(0, i) for i in range(n)], dtype=i32), block_tables=None),
+               dict(is_prefill=True, input_ids=torch.tensor(b_new), positions=torch.arange(256, len(b)),
+                    cu_seqlens=torch.tensor([0, len(b_new)], dtype=i32), cu_seqlens_k=torch.tensor([0, len(b)], dtype=i32),
+                    slot_mapping=torch.tensor([slot(1, i) for i in range(256, len(b))], dtype=i32),
+                    block_tables=torch.tensor([tables[1]], dtype=i32))]
+    steps = gold["steps"]
+    for batch, rec in zip(batches, steps[:2]):
+        yield run_step(batch), rec
+    seqs = [a + steps[0]["tokens"], b + steps[1]["tokens"]]
+    for rec in steps[2:]:
+        batch = dict(is_prefill=False, input_ids=torch.tensor([s[-1] for s in seqs]),
+                     positions=torch.tensor([len(s) - 1 for s in seqs]),
+                     slot_mapping=torch.tensor([slot(r, len(s) - 1) for r, s in enumerate(seqs)], dtype=i32),
+                     context_lens=torch.tensor([len(s) for s in seqs], dtype=i32),
+                     block_tables=torch.tensor(tables, dtype=i32))
+        yield run_step(batch), rec
+        for r, t in enumerate(rec["tokens"]):
+            seqs[r].append(t)
+
+
+def model_step(model, b: dict, device=None):
+    """One forward of a product model (kavor_b200.models) over a replay batch:
+    the batch's tensors moved to ``device``, the attention context set as
+    ModelRunner.prepare_prefill / prepare_decode set it (cu_seqlens_k and
+    block_tables for a prefill over cached blocks), logits returned."""
+    from kavor_b200.utils.context import reset_context, set_context
+
+    if device is not None:
+        b = {k: v.to(device) if isinstance(v, torch.Tensor) else v for k, v in b.items()}
+    if b["is_prefill"]:
+        cu_q = b["cu_seqlens"]
+        cu_k = b.get("cu_seqlens_k", cu_q)
+        set_context(True, cu_q, cu_k, int((cu_q[1:] - cu_q[:-1]).max()), int((cu_k[1:] - cu_k[:-1]).max()),
+                    b["slot_mapping"], None, b.get("block_tables"))
+    else:
+        set_context(False, slot_mapping=b["slot_mapping"], context_lens=b["context_lens"],
+                    block_tables=b["block_tables"])
+    try:
+        with torch.inference_mode():
+            return model.compute_logits(model(b["input_ids"], b["positions"]))
+    finally:
+        reset_context()

@@ -22,10 +22,13 @@ What runs is the reference's own code on the CPU:
   (scheduler.py, block_manager.py, model_runner.py:385-473) on a scripted
   request stream, with the CUDA uploads turned into CPU no-ops;
 * MistralForCausalLM and Ernie4_5ForCausalLM (mistral.py, ernie4_5.py) on
-  tiny configs, the same greedy run as the Qwen3 model.
+  tiny configs, the same greedy run as the Qwen3 model;
+* the Qwen3 model over a cached prefix: a second prompt that reuses the
+  first prompt's full block prefills only its new tokens against the paged
+  cache, then both decode.
 
 Outputs: ops_golden.pt, layer_golden.pt, tiny_model_golden.pt, tiny_model_golden_32.pt,
-mistral_tiny_golden.pt, ernie4_5_tiny_golden.pt, host_trace.json.
+mistral_tiny_golden.pt, ernie4_5_tiny_golden.pt, prefix_cache_golden.pt, host_trace.json.
 """
 from __future__ import annotations
 
@@ -255,6 +258,59 @@ def _greedy_run(model, hkv: int, decode_steps: int, keep_logits: bool) -> dict:
     return dict(prompts=prompts, tables=tables, steps=steps)
 
 
+def golden_prefix_cache() -> dict:
+    """The 2-layer Qwen3 (reference model class, CPU) over a cached prefix:
+    prompt A (300 tokens, blocks [0, 1]) is prefilled; prompt B = A's first 256
+    tokens + 40 new ones reuses block 0 (block table [0, 2]) and prefills only
+    its 40 new tokens against the paged cache (flash_attention_kvcache.py:74-79
+    with block_table); then A and B decode 4 greedy steps together."""
+    from kavor.models.qwen3 import Qwen3ForCausalLM
+    from kavor.utils.context import reset_context, set_context
+
+    shape = cases.TINY
+    model = _ref_model(Qwen3ForCausalLM, cases.hf_config(shape), cases.checkpoint(shape, seed=5))
+    pool = torch.zeros(8, 2, 256, shape["num_key_value_heads"], 128, dtype=torch.bfloat16)
+    pools = [pool.clone() for _ in model.model.layers]
+    for lyr, pl in zip(model.model.layers, pools):
+        lyr.self_attn.attn.k_cache = [pl[:, 0]]
+        lyr.self_attn.attn.v_cache = [pl[:, 1]]
+    a_prompt, b_new = cases.prefix_cache_prompts()
+    b_prompt = a_prompt[:256] + b_new
+    tables = [[0, 1], [0, 2]]
+    i32 = torch.int32
+    steps = []
+    with torch.no_grad():
+        # prefill A
+        n = len(a_prompt)
+        set_context(True, torch.tensor([0, n], dtype=i32), torch.tensor([0, n], dtype=i32), n, n,
+                    torch.tensor([tables[0][i // 256] * 256 + i % 256 for i in range(n)], dtype=i32), None, None)
+        logits = model.compute_logits(model(torch.tensor(a_prompt), torch.arange(n)))
+        reset_context()
+        steps.append(_step_record(logits, True))
+        # prefill B's new tokens over the cached prefix (block 0)
+        nq, nk = len(b_new), len(b_prompt)
+        set_context(True, torch.tensor([0, nq], dtype=i32), torch.tensor([0, nk], dtype=i32), nq, nk,
+                    torch.tensor([tables[1][i // 256] * 256 + i % 256 for i in range(256, nk)], dtype=i32), None,
+                    torch.tensor([tables[1]], dtype=i32))
+        logits = model.compute_logits(model(torch.tensor(b_new), torch.arange(256, nk)))
+        reset_context()
+        steps.append(_step_record(logits, True))
+        seqs = [a_prompt + steps[0]["tokens"], b_prompt + steps[1]["tokens"]]
+        for _ in range(4):
+            ids = torch.tensor([p[-1] for p in seqs])
+            pos = torch.tensor([len(p) - 1 for p in seqs])
+            ctx = torch.tensor([len(p) for p in seqs], dtype=i32)
+            slots = torch.tensor([tables[b][(len(p) - 1) // 256] * 256 + (len(p) - 1) % 256 for b, p in enumerate(seqs)],
+                                 dtype=i32)
+            set_context(False, slot_mapping=slots, context_lens=ctx, block_tables=torch.tensor(tables, dtype=i32))
+            logits = model.compute_logits(model(ids, pos))
+            reset_context()
+            steps.append(_step_record(logits, True))
+            for b, t in enumerate(steps[-1]["tokens"]):
+                seqs[b].append(t)
+    return dict(a_prompt=a_prompt, b_new=b_new, tables=tables, steps=steps)
+
+
 def _step_record(logits: torch.Tensor, keep_logits: bool) -> dict:
     top2 = logits.float().topk(2, dim=-1).values
     rec = dict(tokens=logits.float().argmax(-1).tolist(), margins=(top2[:, 0] - top2[:, 1]).tolist())
@@ -342,6 +398,7 @@ def main() -> int:
     torch.save(golden_tiny_model(decode_steps=31, keep_logits=False), out / "tiny_model_golden_32.pt")
     for family in cases.FAMILIES:
         torch.save(golden_family_model(family), out / f"{family}_tiny_golden.pt")
+    torch.save(golden_prefix_cache(), out / "prefix_cache_golden.pt")
     (out / "host_trace.json").write_text(json.dumps(golden_host_trace()))
     dist.destroy_process_group()
     for f in sorted(out.glob("*golden*")) + [out / "host_trace.json"]:

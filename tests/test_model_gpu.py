@@ -107,7 +107,6 @@ def test_family_model_replays_reference_greedy(family):
     the greedy token wherever the reference's top two logits are more than two
     bf16 ulps apart."""
     from kavor_b200.models import AutoModelForCausalLM
-    from kavor_b200.utils.context import reset_context, set_context
 
     cfg = cases.family_config(family)
     model = _build(lambda: AutoModelForCausalLM.model_class(cfg)(cfg))
@@ -117,23 +116,31 @@ def test_family_model_replays_reference_greedy(family):
         lyr.self_attn.attn.k_cache = [pool[:, 0]]
         lyr.self_attn.attn.v_cache = [pool[:, 1]]
 
-    def step(b):
-        b = {k: v.to(DEV) if isinstance(v, torch.Tensor) else v for k, v in b.items()}
-        if b["is_prefill"]:
-            n = int((b["cu_seqlens"][1:] - b["cu_seqlens"][:-1]).max())
-            set_context(True, b["cu_seqlens"], b["cu_seqlens"], n, n, b["slot_mapping"])
-        else:
-            set_context(False, slot_mapping=b["slot_mapping"], context_lens=b["context_lens"],
-                        block_tables=b["block_tables"])
-        try:
-            with torch.inference_mode():
-                return model.compute_logits(model(b["input_ids"], b["positions"]))
-        finally:
-            reset_context()
-
     gold = torch.load(GOLDEN / f"{family}_tiny_golden.pt", weights_only=False)
-    checked = sum(cases.check_greedy_step(logits, rec) for logits, rec in cases.replay(gold, step))
+    checked = sum(cases.check_greedy_step(logits, rec)
+                  for logits, rec in cases.replay(gold, lambda b: cases.model_step(model, b, DEV)))
     assert checked >= 13  # at least half of the 27 tokens
+
+
+def test_prefix_cache_prefill_replays_reference_greedy():
+    """A prompt whose first 256-token block is already in the cache prefills
+    only its 40 new tokens: the paged prefill attention reads the cached block
+    through the block table (cu_seqlens_k 296 > cu_seqlens_q 40); then both
+    prompts decode 4 steps. Logits cosine >= 0.999 and the reference model's
+    greedy token at every step."""
+    from kavor_b200.models import AutoModelForCausalLM
+
+    cfg = cases.hf_config(cases.TINY)
+    model = _build(lambda: AutoModelForCausalLM.model_class(cfg)(cfg))
+    _load(model, cases.checkpoint(cases.TINY, seed=5), model.packed_modules_mapping)
+    for lyr in model.model.layers:
+        pool = torch.zeros(8, 2, 256, 2, 128, dtype=torch.bfloat16, device=DEV)
+        lyr.self_attn.attn.k_cache = [pool[:, 0]]
+        lyr.self_attn.attn.v_cache = [pool[:, 1]]
+    gold = torch.load(GOLDEN / "prefix_cache_golden.pt", weights_only=False)
+    checked = sum(cases.check_greedy_step(logits, rec)
+                  for logits, rec in cases.replay_prefix_cache(gold, lambda b: cases.model_step(model, b, DEV)))
+    assert checked >= 9  # of 10
 
 
 @pytest.fixture(scope="module")

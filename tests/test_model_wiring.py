@@ -101,8 +101,6 @@ def gemm_backend(request, monkeypatch):
 
 @pytest.mark.parametrize("family,fixture", CASES, ids=[c[0] for c in CASES])
 def test_model_classes_replay_reference_greedy(oracle_kernels, gemm_backend, family, fixture):
-    from kavor_b200.utils.context import reset_context, set_context
-
     cfg = cases.hf_config(cases.TINY) if family == "qwen3" else cases.family_config(family)
     model = _model(cfg)
     for lyr in model.model.layers:
@@ -110,25 +108,29 @@ def test_model_classes_replay_reference_greedy(oracle_kernels, gemm_backend, fam
         lyr.self_attn.attn.k_cache = [pool[:, 0]]
         lyr.self_attn.attn.v_cache = [pool[:, 1]]
 
-    def step(b):
-        if b["is_prefill"]:
-            n = int((b["cu_seqlens"][1:] - b["cu_seqlens"][:-1]).max())
-            set_context(True, b["cu_seqlens"], b["cu_seqlens"], n, n, b["slot_mapping"])
-        else:
-            set_context(False, slot_mapping=b["slot_mapping"], context_lens=b["context_lens"],
-                        block_tables=b["block_tables"])
-        try:
-            with torch.inference_mode():
-                return model.compute_logits(model(b["input_ids"], b["positions"]))
-        finally:
-            reset_context()
-
     gold = torch.load(GOLDEN / fixture, weights_only=False)
     # with the oracle's kernels the logits differ from the reference's only by
     # matmul summation order (cosine > 0.99998 here), so the bound is tighter
     # than the GPU's 0.999: a wrong rope theta or rotation stays above 0.998
-    checked = sum(cases.check_greedy_step(logits, rec, min_cos=0.9999) for logits, rec in cases.replay(gold, step))
+    checked = sum(cases.check_greedy_step(logits, rec, min_cos=0.9999)
+                  for logits, rec in cases.replay(gold, lambda b: cases.model_step(model, b)))
     assert checked >= 13  # at least half of the 27 tokens
+
+
+def test_model_classes_prefix_cache_prefill(oracle_kernels):
+    """The prefill of a prompt whose first block is already cached: the
+    attention layer reads K/V from the paged cache through the block table
+    (cu_seqlens_k > cu_seqlens_q), as ModelRunner.prepare_prefill sets it up."""
+    cfg = cases.hf_config(cases.TINY)
+    model = _model(cfg)
+    for lyr in model.model.layers:
+        pool = torch.zeros(8, 2, 256, cfg.num_key_value_heads, 128, dtype=torch.bfloat16)
+        lyr.self_attn.attn.k_cache = [pool[:, 0]]
+        lyr.self_attn.attn.v_cache = [pool[:, 1]]
+    gold = torch.load(GOLDEN / "prefix_cache_golden.pt", weights_only=False)
+    checked = sum(cases.check_greedy_step(logits, rec, min_cos=0.9999)
+                  for logits, rec in cases.replay_prefix_cache(gold, lambda b: cases.model_step(model, b)))
+    assert checked >= 9  # of 10
 
 
 def test_gemm_backend_names():

@@ -171,6 +171,30 @@ def test_family_model_greedy_matches_reference_model(family):
     assert checked >= 13  # at least half of the 27 tokens (the random-init logits are flat)
 
 
+def test_prefix_cache_prefill_matches_reference_model():
+    """A second prompt that reuses the first one's cached block prefills only
+    its 40 new tokens against the paged cache (block table given, cu_seqlens_k
+    > cu_seqlens_q), then both decode: logits cosine >= 0.999 and the greedy
+    tokens of the reference model at every step."""
+    gold = _load("prefix_cache_golden.pt")
+    shape = omodel.Shape(hidden=512, inter=1024, layers=2, hq=4, hkv=2, vocab=4096)
+    p = cases.checkpoint(cases.TINY, seed=5)
+    kv = [(torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16), torch.zeros(8, 256, 2, 128, dtype=torch.bfloat16))
+          for _ in range(2)]
+
+    def step(b):
+        if b["is_prefill"]:
+            batch = omodel.Batch(True, b["positions"], b["slot_mapping"], b["cu_seqlens"], b["cu_seqlens_k"],
+                                 block_tables=b["block_tables"])
+        else:
+            batch = omodel.Batch(False, b["positions"], b["slot_mapping"], context_lens=b["context_lens"],
+                                 block_tables=b["block_tables"])
+        return omodel.forward(p, b["input_ids"], batch, kv, shape)[1]
+
+    checked = sum(cases.check_greedy_step(logits, rec) for logits, rec in cases.replay_prefix_cache(gold, step))
+    assert checked >= 9  # of 10
+
+
 def test_philox_known_answer():
     """Philox4x32-10 known-answer vectors of the Random123 distribution
     (kat_vectors: counter 0, key 0 and counter/key all-ones)."""

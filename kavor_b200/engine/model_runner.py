@@ -358,6 +358,14 @@ class ModelRunner:
             ev.set()
 
     def call(self, method: str, *args):
+        """Run `method` on every rank (model_runner.py:108-112). A model step
+        ("run", "run_async") has its batch metadata built once, here on rank 0,
+        and the workers receive those arrays (a few KB for a decode step)
+        instead of the pickled sequences, so they neither unpickle the
+        sequences nor rebuild the metadata."""
+        if method in ("run", "run_async"):
+            seqs, arg = args
+            method, args = method + "_step", self._step_metadata(seqs, arg if method == "run" else False) + (arg,)
         if self.world_size > 1 and self.rank == 0 and self.shm is not None:
             self.write_shm(method, *args)
         return getattr(self, method)(*args)
@@ -517,12 +525,24 @@ class ModelRunner:
             raise RuntimeError(f"rank {self.rank}: device-side error bits {bits:#x} ({what}) within the last "
                                f"{self.DEVICE_CHECK_EVERY} steps")
 
-    @torch.inference_mode()
-    def run(self, seqs: list[Sequence], is_prefill: bool) -> list[int]:
-        self._check_device()
+    def _step_metadata(self, seqs: list[Sequence], is_prefill: bool) -> tuple[dict, np.ndarray]:
+        """The host arrays of one model step: prefill_metadata / decode_metadata
+        and the sampling temperatures."""
         temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
         if is_prefill:
-            meta = prefill_metadata(seqs, self.block_size)
+            return prefill_metadata(seqs, self.block_size), temps
+        return decode_metadata(seqs, self.block_size), temps
+
+    def run(self, seqs: list[Sequence], is_prefill: bool) -> list[int]:
+        """One model step of `seqs` (model_runner.py:247-263): the sampled token
+        of every sequence."""
+        return self.run_step(*self._step_metadata(seqs, is_prefill), is_prefill)
+
+    @torch.inference_mode()
+    def run_step(self, meta: dict, temps: np.ndarray, is_prefill: bool) -> list[int]:
+        """``run`` from the step's metadata arrays (what a TP worker receives)."""
+        self._check_device()
+        if is_prefill:
             arrays = [meta["input_ids"], meta["positions"], meta["cu_seqlens_q"], meta["cu_seqlens_k"],
                       meta["slot_mapping"], temps]
             if meta["block_tables"] is not None:
@@ -538,16 +558,15 @@ class ModelRunner:
             finally:
                 reset_context()
             return tokens.tolist()
-        bs = self._decode_launch(seqs, temps, mirror=0, chain=False)
+        bs = self._decode_launch(meta, temps, mirror=0, chain=False)
         return self.decode_buffers.sampled[:bs].tolist()
 
-    def _decode_launch(self, seqs: list[Sequence], temps: np.ndarray, mirror: int, chain) -> int:
+    def _decode_launch(self, meta: dict, temps: np.ndarray, mirror: int, chain) -> int:
         """Upload one decode step's metadata (through pinned mirror `mirror`),
         optionally take the input tokens from the previous step's samples on
         the device (chain True: row i from row i; a list: row i from row
         chain[i]), and launch the step (graph replay, or eager)."""
-        meta = decode_metadata(seqs, self.block_size)
-        bs = len(seqs)
+        bs = len(temps)
         self._ensure_decode_buffers()
         buf = self.decode_buffers
         if bs > buf.max_bs or meta["block_tables"].shape[1] > buf.max_blocks:
@@ -579,8 +598,11 @@ class ModelRunner:
                 reset_context()
         return bs
 
-    @torch.inference_mode()
     def run_async(self, seqs: list[Sequence], chain: bool | list[int] = False) -> PendingDecode | None:
+        return self.run_async_step(*self._step_metadata(seqs, False), chain)
+
+    @torch.inference_mode()
+    def run_async_step(self, meta: dict, temps: np.ndarray, chain: bool | list[int] = False) -> PendingDecode | None:
         """One decode step, issued without waiting for it (no reference
         counterpart; ``run`` is the reference's synchronous call). With
         ``chain``, every sequence's input token is the token the previous
@@ -600,13 +622,13 @@ class ModelRunner:
         prev = self._pending[k]
         if prev is not None and not prev.done and not mailbox_worker:
             raise RuntimeError("run_async: the result of the step issued two calls ago has not been read")
-        if chain is True and len(seqs) != self._async_bs:
+        n = len(temps)
+        if chain is True and n != self._async_bs:
             raise RuntimeError(f"run_async: a chained step needs the previous step's {self._async_bs} sequences")
-        if isinstance(chain, list) and (len(chain) != len(seqs) or not all(0 <= i < self._async_bs for i in chain)):
+        if isinstance(chain, list) and (len(chain) != n or not all(0 <= i < self._async_bs for i in chain)):
             raise RuntimeError(f"run_async: the chain map must give every sequence a row of the previous "
                                f"{self._async_bs}-sequence step")
-        temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
-        bs = self._decode_launch(seqs, temps, mirror=1 + k, chain=chain)
+        bs = self._decode_launch(meta, temps, mirror=1 + k, chain=chain)
         self._async_bs = bs
         if mailbox_worker:
             return None

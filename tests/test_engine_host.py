@@ -246,7 +246,7 @@ def test_runner_forwards_run_under_inference_mode():
     create are inference tensors, and an in-place update of one outside
     inference mode (the sampler seed restore after capture) raises."""
     from kavor_b200.engine.model_runner import ModelRunner
-    for name in ("_profile_prefill", "_profile_decode", "capture_cudagraph", "run"):
+    for name in ("_profile_prefill", "_profile_decode", "capture_cudagraph", "run_step", "run_async_step"):
         assert hasattr(getattr(ModelRunner, name), "__wrapped__"), name
 
 
@@ -391,3 +391,16 @@ def test_shared_prefix_workload_shape():
     assert all(p[:2048] == prefix and 512 <= len(p) - 2048 <= 6144 for p in prompts)
     assert all(0 <= t <= 10000 for p in prompts for t in p)
     assert len({tuple(p[2048:2060]) for p in prompts}) == 64
+
+
+def test_profile_host_runs(capsys):
+    """The host-step profile (schedule, metadata, postprocess, TP message
+    forms, pipelined step) runs on the CPU and reports every field."""
+    import json
+
+    from kavor_b200 import profile_host
+
+    assert profile_host.main(["--batch", "8", "--context", "300", "--steps", "5"]) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    for k in ("schedule", "metadata", "postprocess", "tp_message_sequences", "tp_message_metadata", "pipeline_step"):
+        assert line[k] > 0, k

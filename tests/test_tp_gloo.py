@@ -210,6 +210,73 @@ def test_mailbox_writes_wait_for_a_slow_worker():
         shm.unlink()
 
 
+def test_model_steps_reach_workers_as_metadata_arrays():
+    """ModelRunner.call("run" / "run_async", seqs, ...) on rank 0 builds the
+    step's metadata once and sends the arrays: the worker receives the
+    prefill_metadata / decode_metadata of the same sequences (and their
+    temperatures) bit for bit, and rank 0 runs its own step from them."""
+    import multiprocessing as mp
+    from multiprocessing.shared_memory import SharedMemory
+
+    import numpy as np
+
+    from kavor_b200.engine.model_runner import SHM_BYTES, ModelRunner, decode_metadata, prefill_metadata
+    from kavor_b200.engine.sequence import Sequence
+    from kavor_b200.sampling_params import SamplingParams
+
+    ctx = mp.get_context("spawn")
+    name = f"kvb_meta_{os.getpid()}"
+    shm = SharedMemory(name=name, create=True, size=SHM_BYTES)
+    try:
+        ev = ctx.Event()
+        recv, send = ctx.Pipe(duplex=False)
+        p = ctx.Process(target=_mailbox_worker, args=(name, ev, send))
+        p.start()
+        try:
+            runner = ModelRunner.__new__(ModelRunner)
+            runner.shm, runner.event, runner.world_size, runner.rank, runner.block_size = shm, [ev], WORLD, 0, 256
+            local = []
+            runner.run_step = lambda *a: local.append(("run_step", a)) or [0]
+            runner.run_async_step = lambda *a: local.append(("run_async_step", a))
+            seqs = [Sequence(list(range(1, 300 + 7 * i)), SamplingParams(temperature=0.5 + i, max_tokens=9))
+                    for i in range(3)]
+            for i, s in enumerate(seqs):
+                s.block_table = [2 * i, 2 * i + 1]
+                s.num_scheduled_tokens = s.num_tokens - 256 * (i == 1)  # sequence 1 has a cached first block
+                s.num_cached_tokens = 256 * (i == 1)
+            want_prefill = prefill_metadata(seqs, 256)
+            runner.call("run", seqs, True)
+            for s in seqs:
+                s.num_cached_tokens, s.is_prefill = s.num_tokens, False
+                s.append_token(40 + s.seq_id % 7)
+            want_decode = decode_metadata(seqs, 256)
+            runner.call("run", seqs, False)
+            runner.call("run_async", seqs, [2, 0, 1])
+            ModelRunner.write_shm(runner, "exit")
+            assert recv.poll(60), "the worker never saw its exit message"
+            calls = recv.recv()
+            p.join(timeout=60)
+            assert p.exitcode == 0
+        finally:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
+        temps = np.array([0.5, 1.5, 2.5], np.float32)
+        expect = [("run_step", (want_prefill, temps, True)), ("run_step", (want_decode, temps, False)),
+                  ("run_async_step", (want_decode, temps, [2, 0, 1]))]
+        assert [m for m, _ in calls] == [m for m, _ in expect] + ["exit"]
+        for (m, got), (_, (meta, t, last)), (lm, mine) in zip(calls, expect, local):
+            assert lm == m
+            for args in (tuple(got), mine):
+                assert args[2] == last and np.array_equal(args[1], t)
+                assert args[0].keys() == meta.keys()
+                for k, v in meta.items():
+                    assert (args[0][k] is None) if v is None else np.array_equal(args[0][k], v), (m, k)
+    finally:
+        shm.close()
+        shm.unlink()
+
+
 def test_allreduce_buffer_schedule_never_reuses_consecutively():
     """The decode step's 2L+1 fused all-reduces alternate data buffers so two
     consecutive reductions (also across steps) never share one."""

@@ -88,10 +88,12 @@ __device__ __forceinline__ Best block_argmax(Best b) {
 // -log(-log(u)) <= -log(2^-24) = 24 ln 2 = 16.64 (plus margin for logf).
 constexpr float kGumbelMax = 16.7f;
 
+__device__ __forceinline__ float gumbel_of(uint32_t r) { return -logf(-logf(to_unit(r))); }
+
 __device__ __forceinline__ float gumbel_at(uint64_t n, uint32_t seed) {
   uint32_t r[4];
   philox4x32_10((uint32_t)(n >> 2), (uint32_t)(n >> 34), seed, 0u, r);
-  return -logf(-logf(to_unit(r[n & 3])));
+  return gumbel_of(r[n & 3]);
 }
 
 // Scores one row segment [0, n) whose column j has global index gcol0 + j in a
@@ -127,17 +129,40 @@ __device__ Best score_segment(const bf16* __restrict__ row, int n, int64_t gcol0
   __syncthreads();
   const float bound = bound_s;
   best = {-INFINITY, INT64_MAX};
-  // pass 2: noise for the candidates only
+  // pass 2: noise for the candidates only. One Philox block gives the noise
+  // of 4 consecutive global columns (counter n / 4, lane n % 4): when the
+  // 8 columns of a 16-byte chunk start at a multiple of 4, two blocks serve
+  // all 8 instead of one block per column (the same values either way).
   for (int c = threadIdx.x; c < nv; c += kThreads) {
     const uint4 raw = reinterpret_cast<const uint4*>(row)[c];
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float l[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 p = __bfloat1622float2(h[j]);
-      const float l0 = p.x * inv_t, l1 = p.y * inv_t;
-      const int64_t g0 = gcol0 + c * 8 + 2 * j;
-      if (l0 >= bound) take(best, l0 + gumbel_at((uint64_t)(row_base + g0), seed), g0);
-      if (l1 >= bound) take(best, l1 + gumbel_at((uint64_t)(row_base + g0 + 1), seed), g0 + 1);
+      l[2 * j] = p.x * inv_t;
+      l[2 * j + 1] = p.y * inv_t;
+    }
+    const int64_t g0 = gcol0 + c * 8;
+    const uint64_t n0 = (uint64_t)(row_base + g0);
+    if ((n0 & 3) == 0) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        bool any = false;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) any |= l[4 * q + k] >= bound;
+        if (!any) continue;
+        const uint64_t n = n0 + 4 * q;
+        uint32_t r[4];
+        philox4x32_10((uint32_t)(n >> 2), (uint32_t)(n >> 34), seed, 0u, r);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (l[4 * q + k] >= bound) take(best, l[4 * q + k] + gumbel_of(r[k]), g0 + 4 * q + k);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (l[k] >= bound) take(best, l[k] + gumbel_at(n0 + k, seed), g0 + k);
     }
   }
   for (int j = nv * 8 + threadIdx.x; j < n; j += kThreads) {

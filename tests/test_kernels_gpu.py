@@ -290,6 +290,36 @@ def test_sampler_gumbel_matches_oracle_philox():
             assert abs(scores[b, tok[b]].item() - scores[b, ref[b]].item()) < 1e-4, b
 
 
+def test_sampler_gumbel_unaligned_noise_counters():
+    """Rows whose global column counter does not start at a multiple of 4
+    (vocab 3002 in rows of stride 3008, and a shard at column offset 1001):
+    the 16-byte chunks take the per-column noise path, the aligned rows the
+    4-columns-per-Philox-block path; both draw the oracle's noise."""
+    B, V, S = 16, 3002, 3008
+    full = (torch.randn(B, S, generator=g(54)) * 2).to(torch.bfloat16)
+    logits = full[:, :V]
+    temps = torch.tensor([0.6, 1.0, 1.3, 0.9] * (B // 4), dtype=torch.float32)
+    seed = 4321
+    dseed = torch.tensor(seed, dtype=torch.int32, device=DEV)
+    tok = K().sample(full.to(DEV)[:, :V], temps.to(DEV), dseed).cpu()
+    scores = ops.gumbel_scores(logits, temps, seed)
+    ref = ops.sample(logits, temps, seed)
+    for b in range(B):
+        if tok[b] != ref[b]:
+            assert abs(scores[b, tok[b]].item() - scores[b, ref[b]].item()) < 1e-4, b
+    # the shard [1001, 3001) of the same rows, scored with its global columns
+    off, n = 1001, 2000
+    shard = full[:, off:off + n].contiguous().to(DEV)
+    val = torch.empty(B, dtype=torch.float32, device=DEV)
+    idx = torch.empty(B, dtype=torch.int64, device=DEV)
+    K().sample_partial(shard, temps.to(DEV), dseed, off, V, val, idx)
+    best = scores[:, off:off + n].argmax(-1) + off
+    for b in range(B):
+        got = int(idx[b])
+        if got != int(best[b]):
+            assert abs(scores[b, got].item() - scores[b, best[b]].item()) < 1e-4, b
+
+
 def test_sampler_distribution_matches_softmax():
     V, N = 50, 20000
     logits = (torch.randn(V, generator=g(52)) * 4).to(torch.bfloat16)

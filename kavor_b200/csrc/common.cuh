@@ -206,15 +206,18 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ---------------------------------------------------- programmatic dependent launch
-// Every kernel starts with kernel_entry(): wait until the grids it depends on
+// Every kernel calls kernel_entry() before its first access to memory that
+// another kernel writes (at its start, or after its set-up): wait until the grids it depends on
 // have completed and their writes are visible (griddepcontrol.wait; returns at
 // once when the kernel was launched without a programmatic dependency). With
 // programmatic launch on (kvb_set_pdl), it then lets the next kernel of the
 // stream be scheduled early (it stops at its own wait), so that kernel's launch
 // and CTA dispatch overlap this kernel's run; off (the default), the next
-// kernel starts after this one ends, as with plain launches. Nothing touches
-// global memory before the wait. The switch is a per-translation-unit
-// constant, written by kvb_set_pdl through set_pdl_trigger_<tag>().
+// kernel starts after this one ends, as with plain launches. Nothing that a
+// kernel before it writes is read, and nothing is written, before the wait
+// (the GEMM requests its first weight tiles, which no kernel writes, before
+// it). The switch is a per-translation-unit constant, written by kvb_set_pdl
+// through set_pdl_trigger_<tag>().
 static __constant__ int c_pdl_trigger = 0;
 
 __device__ __forceinline__ void kernel_entry() {

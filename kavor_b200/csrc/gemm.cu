@@ -206,7 +206,6 @@ template <int MT, bool G, bool CL>
 __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                 const __grid_constant__ GemmArgs a) {
-  kernel_entry();
   using C = Cfg<MT, G, CL>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -229,6 +228,25 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
     }
     fence_barrier_init();
   }
+  // Launched programmatically (kvb_set_pdl), this kernel may start while the
+  // kernel before it still runs: the weights are not that kernel's output, so
+  // the producer (thread 0) requests the weight tiles of its first unit's first
+  // K-steps into the stage ring now, and only the token tiles wait for the
+  // grid dependency. Without programmatic launch nothing is issued early.
+  int pre = 0;  // K-steps whose weight tiles are already requested (thread 0)
+  if (threadIdx.x == 0 && c_pdl_trigger && (int)blockIdx.x < a.units) {
+    prefetch_tensormap(&wmap);
+    int n_tile, m_tile, split, kb0, nkb;
+    unit_coords(a, blockIdx.x, n_tile, m_tile, split, kb0, nkb);
+    pre = nkb < S ? nkb : S;
+    for (int i = 0; i < pre; ++i) {
+      const uint32_t sa = smem_u32(smem + i * C::kStageBytes);
+      const uint32_t fb = smem_u32(&full_bar[i]);
+      mbar_arrive_expect_tx(fb, C::kStageBytes);
+      tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n_tile * kBN, fb);
+      if constexpr (G) tma_load_2d(sa + kABytes, &wmap, (kb0 + i) * kBK, a.up_row0 + n_tile * kBN, fb);
+    }
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
                  "r"(C::kTmemCols)
@@ -238,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  kernel_entry();  // the token tiles and every output row come after the grid dependency
   const uint32_t tmem = tmem_base_s;
   bool dead = false;  // a bounded wait gave up: skip the work, keep every barrier balanced
 
@@ -266,9 +285,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<MT, G, CL>::kPerSm)
           }
           const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
           const uint32_t fb = smem_u32(&full_bar[s]);
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
-          tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n_tile * kBN, fb);
-          if constexpr (G) tma_load_2d(sa + kABytes, &wmap, (kb0 + i) * kBK, a.up_row0 + n_tile * kBN, fb);
+          if (it >= pre) {  // (the first `pre` steps' weights were requested before the grid dependency)
+            mbar_arrive_expect_tx(fb, C::kStageBytes);
+            tma_load_2d(sa, &wmap, (kb0 + i) * kBK, n_tile * kBN, fb);
+            if constexpr (G) tma_load_2d(sa + kABytes, &wmap, (kb0 + i) * kBK, a.up_row0 + n_tile * kBN, fb);
+          }
           tma_load_2d(sa + C::kA * kABytes, &xmap, (kb0 + i) * kBK, m_tile * MT, fb);
           const int j = i + a.pf;
           if (a.pf > 0 && j < nkb && j >= first) {

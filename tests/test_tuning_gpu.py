@@ -199,21 +199,25 @@ def test_tcgen05_gemm_backend_replays_reference_greedy(prefetch):
     assert checked >= 13
 
 
-def test_programmatic_dependent_launch_changes_no_result(tiny_dir):
+@pytest.mark.parametrize("gemm", ["cublas", "tcgen05"])
+def test_programmatic_dependent_launch_changes_no_result(tiny_dir, gemm):
     """With every kernel launched as a programmatic dependent (kvb_set_pdl)
     inside and outside the captured decode graphs, greedy decoding gives the
-    same tokens as plain stream-ordered launches: each kernel waits at its
-    start for the one before it."""
+    same tokens as plain stream-ordered launches: each kernel waits for the
+    one before it before reading its output (the package's GEMM requests its
+    first weight tiles, which no kernel writes, before that wait)."""
     from kavor_b200 import _kernels as K_
+    from kavor_b200.layers.linear import set_gemm_backend
 
     runs = []
     for pdl in (False, True):
-        runner = _runner(tiny_dir, pdl=pdl)
+        runner = _runner(tiny_dir, pdl=pdl, gemm_backend=gemm)
         try:
             runs.append(_greedy_decode(runner, False))
         finally:
             runner.exit()
             K_.set_pdl(False)
+            set_gemm_backend("cublas")
     assert runs[0] == runs[1]
 
 

@@ -64,6 +64,8 @@ def parse_args(argv=None):
     ap.add_argument("--pdl", action="store_true", help="programmatic dependent launch of the package's kernels")
     ap.add_argument("--no-probes", action="store_true",
                     help="skip the one-GPU probes of the package's GEMM in place of cuBLAS")
+    ap.add_argument("--microbatches", type=int, choices=[1, 2], default=1,
+                    help="TP > 1: 2 runs the decode step as two halves on two streams (Config.decode_microbatches)")
     ap.add_argument("--e2e-pipelined", action="store_true",
                     help="e2e through ModelRunner.run_async with one step in flight (host work overlaps the GPU)")
     return ap.parse_args(argv)
@@ -251,7 +253,7 @@ def _config(args) -> dict:
     return {"workload": f"{args.model} decode step, batch {args.batch}, context {args.context}, TP={args.gpus}",
             "model": args.model, "global_batch": args.batch, "context": args.context, "block_size": 256,
             "parallelism": f"tp{args.gpus}", "gemm": args.gemm, "gemm_l2_prefetch": args.gemm_l2_prefetch,
-            "pdl": args.pdl, "e2e_pipelined": args.e2e_pipelined,
+            "pdl": args.pdl, "e2e_pipelined": args.e2e_pipelined, "decode_microbatches": args.microbatches,
             "l2": "inputs larger than L2 (per step: all weights + every sequence's KV pages)"}
 
 
@@ -317,7 +319,7 @@ def run_ours(args) -> int:
     cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world, max_model_len=max_len,
                  max_num_seqs=B, max_num_batched_tokens=4096, num_kvcache_blocks=B * blocks_per_seq + 8,
                  rdzv_port=1, graph_batch_sizes=(B,), gemm_backend=args.gemm,
-                 gemm_l2_prefetch=args.gemm_l2_prefetch, pdl=args.pdl)
+                 gemm_l2_prefetch=args.gemm_l2_prefetch, pdl=args.pdl, decode_microbatches=args.microbatches)
     runner = ModelRunner(cfg, rank, None)
     with torch.no_grad():
         runner.cache.pools.view(torch.bfloat16).normal_(0.0, 1.0)  # resident KV pages, N(0, 1)

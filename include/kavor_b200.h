@@ -278,6 +278,15 @@ int kvb_comm_destroy(void* comm);
 int kvb_comm_area_size(size_t max_bytes, size_t* bytes);
 int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t multicast_base, size_t area_bytes,
                     size_t max_bytes, void** comm);
+/* Largest grid (blocks) of this communicator's kvb_allreduce_add_rmsnorm
+ * launches, 1..256 (default 256; a block then handles several rows). Every
+ * rank of the group must set the same value. Each block of a call waits for
+ * the same block of every peer, so all blocks of a call must be resident at
+ * once: a caller that runs two groups' calls concurrently on two streams caps
+ * both, so that the two grids together leave SMs free for the other kernels.
+ * No reference counterpart (the reference issues one NCCL all-reduce at a
+ * time, linear.py:158-159). */
+int kvb_comm_set_max_blocks(void* comm, int max_blocks);
 /* 1 when the communicator has a multicast mapping (switch-reduced modes). */
 int kvb_comm_has_multicast(void* comm);
 /* The exchange kvb_allreduce_add_rmsnorm runs for these arguments (host

@@ -56,6 +56,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_comm_area_size": [c_size_t, POINTER(c_size_t)],
     "kvb_comm_attach": [I, I, POINTER(ctypes.c_uint64), ctypes.c_uint64, c_size_t, c_size_t, POINTER(c_void_p)],
     "kvb_comm_has_multicast": [P],
+    "kvb_comm_set_max_blocks": [P, I],
     "kvb_comm_result_rows": [P, POINTER(c_void_p), POINTER(c_void_p)],
     "kvb_allreduce_plan": [I, I, I, I, I, POINTER(c_int)],
     "kvb_allreduce_add_rmsnorm": [P, I, P, P, P, P, I, I, F, I, P],
@@ -68,7 +69,7 @@ _QUERIES = {
     "kvb_version", "kvb_device_error", "kvb_sm_count", "kvb_paged_decode_attn_workspace_size",
     "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch",
     "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach",
-    "kvb_comm_has_multicast", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
+    "kvb_comm_has_multicast", "kvb_comm_set_max_blocks", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
     "kvb_comm_data_buffer", "kvb_comm_destroy",
 }
 # Number of launching entry-point calls made so far (per name); used to count

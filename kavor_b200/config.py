@@ -7,8 +7,11 @@ caches prefixes), ``graph_batch_sizes`` (the decode batch buckets captured
 as CUDA graphs; default: the reference's 1, 2, 4, 8 and multiples of 16),
 ``fused_allreduce``, ``gemm_backend`` / ``gemm_l2_prefetch`` (which GEMM
 the projections use, and its L2 prefetch distance), ``pdl`` (programmatic
-dependent launch of the package's kernels) and ``async_decode`` (the engine
-keeps one decode step in flight).
+dependent launch of the package's kernels), ``async_decode`` (the engine
+keeps one decode step in flight) and ``decode_microbatches`` /
+``decode_microbatch_min_bs`` (TP > 1: a decode batch of at least that many
+sequences runs as two halves on two streams, each half's all-reduces and
+GEMMs beside the other half's attention).
 """
 from __future__ import annotations
 
@@ -60,6 +63,8 @@ class Config:
     gemm_l2_prefetch: int = 0     # tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads (0 = off)
     pdl: bool = False             # programmatic dependent launch of the package's kernels (kvb_set_pdl)
     async_decode: bool = False    # LLM.generate: one decode step in flight (engine.pipeline.DecodePipeline)
+    decode_microbatches: int = 1  # TP > 1 with the fused all-reduce: 2 = decode as two halves on two streams
+    decode_microbatch_min_bs: int = 64  # smallest decode batch that is split (smaller ones run whole)
 
     def __post_init__(self):
         if not os.path.isdir(self.model):
@@ -69,6 +74,8 @@ class Config:
         assert self.load_format in ("auto", "dummy")
         assert self.gemm_backend in ("cublas", "tcgen05", "tcgen05_pair"), "unknown gemm_backend"
         assert 0 <= self.gemm_l2_prefetch <= 64
+        assert self.decode_microbatches in (1, 2), "decode_microbatches must be 1 or 2"
+        assert self.decode_microbatch_min_bs >= 2
         self.rdzv_port = self.rdzv_port if self.rdzv_port > 0 else free_port()
         if self.hf_config is None:
             self.hf_config = load_hf_config(self.model)

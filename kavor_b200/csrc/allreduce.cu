@@ -54,6 +54,7 @@ struct Comm {
   uint32_t* mc_counters = nullptr;  // [2][kMaxBlocks] calls per block that ran the first / second switch arrival
   bool opened[kMaxRanks] = {};
   bool owns_area = true;    // false: the area was attached (allocated and mapped by the caller)
+  int max_blocks = kMaxBlocks;  // grid cap of a call (kvb_comm_set_max_blocks)
 };
 
 struct Layout {
@@ -547,6 +548,15 @@ extern "C" int kvb_allreduce_plan(int world, int has_multicast, int tokens, int 
   return kOk;
 }
 
+extern "C" int kvb_comm_set_max_blocks(void* comm, int max_blocks) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c || max_blocks < 1 || max_blocks > kMaxBlocks)
+    return set_error(kInvalid, "kvb_comm_set_max_blocks: need a communicator and 1 <= max_blocks <= %d (got %d)",
+                     kMaxBlocks, max_blocks);
+  c->max_blocks = max_blocks;
+  return kOk;
+}
+
 extern "C" int kvb_comm_has_multicast(void* comm) {
   Comm* c = static_cast<Comm*>(comm);
   return c && c->mc ? 1 : 0;
@@ -606,7 +616,7 @@ extern "C" int kvb_allreduce_add_rmsnorm(void* comm, int data_index, const void*
     return set_error(kInvalid, "kvb_allreduce_add_rmsnorm: out / residual_out in the result area need the switch two-shot mode");
   // rows per block: one row (one-shot, peer two-shot) or one group of W rows (switch two-shot)
   const int rows = a.nvls == 2 ? (tokens + c->world - 1) / c->world : tokens;
-  const int blocks = rows < kMaxBlocks ? rows : kMaxBlocks;
+  const int blocks = rows < c->max_blocks ? rows : c->max_blocks;
   const int nch = hidden / 8;
   cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e;

@@ -31,7 +31,7 @@ from kavor_b200 import _kernels as K
 from kavor_b200 import _lib
 from kavor_b200.engine.cache_pool import CachePool
 from kavor_b200.engine.sequence import Sequence
-from kavor_b200.layers.allreduce import TPAllReduce, set_tp_allreduce
+from kavor_b200.layers.allreduce import DecodeMicrobatches, TPAllReduce, set_decode_microbatches, set_tp_allreduce
 from kavor_b200.layers.linear import set_gemm_backend
 from kavor_b200.layers.sampler import Sampler
 from kavor_b200.models import AutoModelForCausalLM
@@ -282,10 +282,18 @@ class ModelRunner:
             self.model = AutoModelForCausalLM.from_pretrained(config.hf_config, load_format=config.load_format,
                                                               seed=config.seed)
             self.tp_allreduce = None
+            self.decode_microbatches = None
             if self.world_size > 1 and config.fused_allreduce:
                 max_tokens = max(config.max_num_batched_tokens, self._max_graph_bs())
                 self.tp_allreduce = TPAllReduce(max_tokens, config.hf_config.hidden_size, self.device)
                 set_tp_allreduce(self.tp_allreduce)
+                if config.decode_microbatches == 2:  # two decode halves, a communicator each
+                    half = (self._max_graph_bs() + 1) // 2
+                    comms = tuple(TPAllReduce(half, config.hf_config.hidden_size, self.device,
+                                              max_blocks=DecodeMicrobatches.MAX_BLOCKS) for _ in range(2))
+                    self.decode_microbatches = DecodeMicrobatches(comms, config.decode_microbatch_min_bs,
+                                                                  torch.cuda.Stream(self.device))
+                    set_decode_microbatches(self.decode_microbatches)
             self.sampler = Sampler()
             self.staging = Staging(self.device)
             self.allocate_kv_cache()
@@ -380,6 +388,10 @@ class ModelRunner:
         self.graphs.clear()
         self.graph_pool = None
         torch.cuda.synchronize()
+        if self.decode_microbatches is not None:
+            set_decode_microbatches(None)
+            self.decode_microbatches.close()
+            self.decode_microbatches = None
         if self.tp_allreduce is not None:
             set_tp_allreduce(None)
             self.tp_allreduce.close()

@@ -17,6 +17,7 @@ the layers alternate 0 and 1).
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import torch
@@ -41,7 +42,7 @@ class TPAllReduce:
     EMBED_BUFFER = 2
 
     def __init__(self, max_tokens: int, hidden: int, device: torch.device, group=None, backend: str = "auto",
-                 mode: int = 0):
+                 mode: int = 0, max_blocks: int | None = None):
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.hidden = hidden
@@ -71,6 +72,8 @@ class TPAllReduce:
         if not self.comm:
             self._create_ipc(max_bytes, group)
         self.multicast = bool(_lib.load().kvb_comm_has_multicast(self.comm))
+        if max_blocks is not None:  # every rank passes the same value
+            _lib.call("kvb_comm_set_max_blocks", self.comm, int(max_blocks))
         self.buffers = []
         for i in range(3):
             ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
@@ -175,7 +178,88 @@ def allreduce_plan(world: int, multicast: bool, tokens: int, hidden: int, mode: 
     return {"peer_two_shot": plan[0], "switch": plan[1]}
 
 
+class DecodeMicrobatches:
+    """Plan of a TP > 1 decode step run as two micro-batches: rows [0, h) on
+    the launching stream, rows [h, T) on a second stream, each half with its
+    own communicator (its all-reduces are ordered on its stream, and two
+    communicators never share flags, counters or buffers). The decode
+    attention kernels of the two halves take turns (each waits for the
+    previous one, whichever half ran it), so one half's attention, bound by
+    HBM bandwidth, runs beside the other half's GEMMs and all-reduces, which
+    are bound by latency at decode sizes.
+
+    Every block of an all-reduce call waits for the same block on every peer,
+    so a call must have all its blocks resident at once; the two halves' calls
+    can be in flight together, so both communicators cap their grids
+    (``max_blocks``) to leave SMs for the other kernels.
+
+    ``streams``: None runs both halves on the current stream (no CUDA: the
+    CPU tests of the wiring), else the second half's stream."""
+
+    MAX_BLOCKS = 64
+
+    def __init__(self, comms: tuple, min_tokens: int, side_stream=None):
+        if len(comms) != 2:
+            raise ValueError("DecodeMicrobatches needs one communicator per half")
+        self.comms = tuple(comms)
+        self.min_tokens = max(2, int(min_tokens))
+        self.side = side_stream
+        self._last = None  # (half, event) of the latest attention
+
+    def applies(self, tokens: int) -> bool:
+        return tokens >= self.min_tokens and all(tokens - tokens // 2 <= c.max_tokens for c in self.comms)
+
+    @staticmethod
+    def spans(tokens: int) -> tuple[tuple[int, int], tuple[int, int]]:
+        h = (tokens + 1) // 2
+        return (0, h), (h, tokens)
+
+    def fork(self) -> None:
+        """Start of a step: the second stream waits for the work issued so far."""
+        self._last = None
+        if self.side is not None:
+            self.side.wait_stream(torch.cuda.current_stream())
+
+    def join(self) -> None:
+        """End of a step: the launching stream waits for the second half."""
+        self._last = None
+        if self.side is not None:
+            torch.cuda.current_stream().wait_stream(self.side)
+
+    def on(self, half: int):
+        """Issue the block's work for micro-batch `half` on its stream."""
+        if half == 0 or self.side is None:
+            return contextlib.nullcontext()
+        return torch.cuda.stream(self.side)
+
+    @contextlib.contextmanager
+    def attention_turn(self, half: int):
+        """Around one half's decode attention: wait until the previous
+        attention (if the other half ran it) is complete, then mark this one."""
+        if self.side is not None and self._last is not None and self._last[0] != half:
+            torch.cuda.current_stream().wait_event(self._last[1])
+        yield
+        if self.side is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+            self._last = (half, ev)
+
+    def close(self, group=None) -> None:
+        for c in self.comms:
+            c.close(group)
+
+
 _TP: TPAllReduce | None = None
+_MICROBATCH: DecodeMicrobatches | None = None
+
+
+def set_decode_microbatches(plan: DecodeMicrobatches | None) -> None:
+    global _MICROBATCH
+    _MICROBATCH = plan
+
+
+def get_decode_microbatches() -> DecodeMicrobatches | None:
+    return _MICROBATCH
 
 
 def set_tp_allreduce(comm: TPAllReduce | None) -> None:

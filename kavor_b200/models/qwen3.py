@@ -13,19 +13,21 @@ same computation with the per-layer work fused into fewer kernels:
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 from torch import nn
 
 from kavor_b200 import _kernels as K
 from kavor_b200.layers.activation import SiluAndMul
-from kavor_b200.layers.allreduce import get_tp_allreduce
+from kavor_b200.layers.allreduce import get_decode_microbatches, get_tp_allreduce
 from kavor_b200.layers.attention import Attention
 from kavor_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
 from kavor_b200.layers.layernorm import RMSNorm
 from kavor_b200.layers.linear import (MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp,
                                       gemm_backend)
 from kavor_b200.layers.rotary_embedding import get_rope
-from kavor_b200.utils.context import get_context
+from kavor_b200.utils.context import context_scope, decode_rows, get_context
 
 
 def rope_theta_of(config, default: float = 1000000.0) -> float:
@@ -75,7 +77,10 @@ class Qwen3Attention(nn.Module):
             self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor, reduce: bool = True,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, attention_turn=None) -> torch.Tensor:
+        """``attention_turn``: an optional context manager entered around the
+        attention kernel alone (a decode step split into micro-batches orders
+        the halves' attention kernels with it)."""
         qkv = self.qkv_proj(hidden_states)
         ctx = get_context()
         k_cache, v_cache = self.attn.k_cache[0], self.attn.v_cache[0]
@@ -90,7 +95,8 @@ class Qwen3Attention(nn.Module):
         q = q.view(-1, self.num_heads, self.head_dim)
         k = k.view(-1, self.num_kv_heads, self.head_dim)
         v = v.view(-1, self.num_kv_heads, self.head_dim)
-        o = self.attn(q, k, v, kv_stored=True)
+        with attention_turn if attention_turn is not None else contextlib.nullcontext():
+            o = self.attn(q, k, v, kv_stored=True)
         return self.o_proj(o.flatten(1, -1), reduce=reduce, out=out)
 
 
@@ -167,6 +173,9 @@ class Qwen3Model(nn.Module):
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         ar = get_tp_allreduce()
         if ar is not None and self.embed_tokens.tp_size > 1:
+            mb = get_decode_microbatches()
+            if mb is not None and not get_context().is_prefill and mb.applies(input_ids.numel()):
+                return self._forward_microbatched(mb, input_ids, positions)
             return self._forward_fused_allreduce(ar, input_ids, positions)
         hidden_states = self.embed_tokens(input_ids)
         residual = None
@@ -194,6 +203,50 @@ class Qwen3Model(nn.Module):
             idx, buf = ar.next_buffer(T)
             layer.mlp(x, reduce=False, out=buf)
         out, _ = ar.reduce_norm(idx, T, residual, self.norm.weight, self.norm.eps)
+        return out
+
+    def _forward_microbatched(self, mb, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        """A TP > 1 decode step as two micro-batches (``DecodeMicrobatches``):
+        the same per-row computation as ``_forward_fused_allreduce``, issued
+        layer by layer for rows [0, h) on the launching stream and rows [h, T)
+        on the second stream, each half with its own communicator and its
+        slices of the step's metadata; the halves' attention kernels take
+        turns. Returns the final normalised rows of both halves in one
+        [T, hidden] tensor."""
+        T = input_ids.numel()
+        spans = mb.spans(T)
+        ctx = get_context()
+        subs = [decode_rows(ctx, lo, hi) for lo, hi in spans]
+        out = torch.empty(T, self.embed_tokens.weight.shape[1], dtype=torch.bfloat16, device=input_ids.device)
+        mb.fork()
+        state = []  # per half: [partial buffer index, residual]
+        for m, (lo, hi) in enumerate(spans):
+            ar = mb.comms[m]
+            with mb.on(m):
+                ar.start_forward()
+                self.embed_tokens(input_ids[lo:hi], reduce=False, out=ar.partial_buffer(ar.EMBED_BUFFER, hi - lo))
+            state.append([ar.EMBED_BUFFER, None])
+        for layer in self.layers:
+            for m, (lo, hi) in enumerate(spans):
+                ar, st, n = mb.comms[m], state[m], hi - lo
+                with mb.on(m), context_scope(subs[m]):
+                    ln = layer.input_layernorm
+                    x, st[1] = ar.reduce_norm(st[0], n, st[1], ln.weight, ln.eps)
+                    st[0], buf = ar.next_buffer(n)
+                    layer.self_attn(positions[lo:hi], x, reduce=False, out=buf, attention_turn=mb.attention_turn(m))
+            for m, (lo, hi) in enumerate(spans):
+                ar, st, n = mb.comms[m], state[m], hi - lo
+                with mb.on(m):
+                    ln = layer.post_attention_layernorm
+                    x, st[1] = ar.reduce_norm(st[0], n, st[1], ln.weight, ln.eps)
+                    st[0], buf = ar.next_buffer(n)
+                    layer.mlp(x, reduce=False, out=buf)
+        for m, (lo, hi) in enumerate(spans):
+            ar, st = mb.comms[m], state[m]
+            with mb.on(m):
+                y, _ = ar.reduce_norm(st[0], hi - lo, st[1], self.norm.weight, self.norm.eps)
+                out[lo:hi].copy_(y)
+        mb.join()
         return out
 
 

@@ -8,6 +8,7 @@ Same fields and semantics as the reference's global context
 """
 from __future__ import annotations
 
+from contextlib import contextmanager
 from dataclasses import dataclass
 
 import torch
@@ -42,3 +43,24 @@ def set_context(is_prefill: bool, cu_seqlens_q=None, cu_seqlens_k=None, max_seql
 def reset_context() -> None:
     global _CONTEXT
     _CONTEXT = Context()
+
+
+@contextmanager
+def context_scope(ctx: Context):
+    """Make `ctx` the current context inside the block (the one before it is
+    restored on exit): a decode step split into row ranges gives each range
+    the slices of the step's metadata."""
+    global _CONTEXT
+    prev, _CONTEXT = _CONTEXT, ctx
+    try:
+        yield ctx
+    finally:
+        _CONTEXT = prev
+
+
+def decode_rows(ctx: Context, lo: int, hi: int) -> Context:
+    """The decode context of rows [lo, hi) of a decode step's context."""
+    if ctx.is_prefill:
+        raise ValueError("decode_rows: prefill contexts are not split by rows")
+    return Context(False, slot_mapping=ctx.slot_mapping[lo:hi], context_lens=ctx.context_lens[lo:hi],
+                   block_tables=ctx.block_tables[lo:hi])

@@ -60,6 +60,9 @@ CASES = [
     ("kvb_comm_create", (2, 2, 1 << 20, ctypes.byref(ctypes.c_void_p()), ctypes.create_string_buffer(64)),
      INVALID, "bad arguments"),
     ("kvb_allreduce_add_rmsnorm", (NULL, 0, NULL, FAKE, FAKE, FAKE, 4, 4096, 1e-6, 0, NULL), INVALID, "bad arguments"),
+    ("kvb_comm_set_max_blocks", (NULL, 64), INVALID, "max_blocks"),
+    ("kvb_comm_set_max_blocks", (FAKE, 0), INVALID, "max_blocks"),
+    ("kvb_comm_set_max_blocks", (FAKE, 257), INVALID, "max_blocks"),
     ("kvb_allreduce_plan", (8, 1, 4, 4096, 9, ctypes.cast(ctypes.create_string_buffer(8), ctypes.POINTER(ctypes.c_int))),
      INVALID, "bad arguments"),
     ("kvb_gemm_plan", (0, 64, 64, 0, 0, ctypes.cast(ctypes.create_string_buffer(16), ctypes.POINTER(ctypes.c_int))),

@@ -51,14 +51,18 @@ def _decode(q, k_cache, v_cache, block_tables, context_lens, scale, out=None, nu
     return ops.paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale)
 
 
+# kernel wrapper name -> its oracle restatement (also used by the gloo TP tests)
+ORACLE_KERNELS = (("qknorm_rope_store", _qknorm_rope_store), ("add_rmsnorm", _add_rmsnorm),
+                  ("rmsnorm", lambda x, w, eps, out=None: ops.rmsnorm(x, w, eps)),
+                  ("silu_mul", lambda x, out=None: ops.silu_mul(x)), ("embedding", _embedding),
+                  ("prefill_attention", _prefill), ("paged_decode_attention", _decode))
+
+
 @pytest.fixture
 def oracle_kernels(monkeypatch):
     from kavor_b200 import _kernels as K
 
-    for name, fn in (("qknorm_rope_store", _qknorm_rope_store), ("add_rmsnorm", _add_rmsnorm),
-                     ("rmsnorm", lambda x, w, eps, out=None: ops.rmsnorm(x, w, eps)),
-                     ("silu_mul", lambda x, out=None: ops.silu_mul(x)), ("embedding", _embedding),
-                     ("prefill_attention", _prefill), ("paged_decode_attention", _decode)):
+    for name, fn in ORACLE_KERNELS:
         monkeypatch.setattr(K, name, fn)
 
 

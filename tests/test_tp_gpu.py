@@ -24,7 +24,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, microbatch=False):
     import datetime
     import sys
 
@@ -57,6 +57,14 @@ def _worker(rank, world, port, results):
             _assign(model, name, t.to(dev), model.packed_modules_mapping, loaded)
         ar = TPAllReduce(1024, cfg.hidden_size, dev)
         set_tp_allreduce(ar)
+        plan = None
+        if microbatch:  # decode steps as two halves (2 + 1 rows) on two streams, a communicator each
+            from kavor_b200.layers.allreduce import DecodeMicrobatches, set_decode_microbatches
+
+            halves = tuple(TPAllReduce(8, cfg.hidden_size, dev, max_blocks=DecodeMicrobatches.MAX_BLOCKS)
+                           for _ in range(2))
+            plan = DecodeMicrobatches(halves, min_tokens=2, side_stream=torch.cuda.Stream(dev))
+            set_decode_microbatches(plan)
         hkv = cfg.num_key_value_heads // world
         pools = [torch.zeros(8, 2, 256, hkv, 128, dtype=torch.bfloat16, device=dev) for _ in range(2)]
         for lyr, pool in zip(model.model.layers, pools):
@@ -99,6 +107,9 @@ def _worker(rank, world, port, results):
         out["backend"] = ar.backend
         out["device_error"] = __import__("kavor_b200._lib", fromlist=["x"]).device_error(clear=True)
         set_tp_allreduce(None)
+        if plan is not None:
+            set_decode_microbatches(None)
+            plan.close()
         ar.close()
     except Exception as e:
         out["error"] = repr(e)
@@ -108,8 +119,17 @@ def _worker(rank, world, port, results):
     results[rank] = out
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_tp_model_matches_oracle(world):
+PENDING = os.environ.get("KVB_GPU_PENDING") != "1"
+
+
+@pytest.mark.parametrize("world,microbatch", [
+    (2, False), (4, False), (8, False),
+    # decode steps split into two micro-batches on two streams: not yet run on
+    # a GPU, so only with KVB_GPU_PENDING=1 until its first run has passed
+    pytest.param(2, True, marks=pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")),
+    pytest.param(8, True, marks=pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")),
+])
+def test_tp_model_matches_oracle(world, microbatch):
     import torch.multiprocessing as mp
 
     import cases
@@ -121,7 +141,7 @@ def test_tp_model_matches_oracle(world):
     with ctx.Manager() as m:
         results = m.dict()
         port = _port()
-        ps = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+        ps = [ctx.Process(target=_worker, args=(r, world, port, results, microbatch)) for r in range(world)]
         for p in ps:
             p.start()
         for p in ps:
@@ -184,3 +204,76 @@ def test_llm_generate_tp2(tmp_path):
         assert all(0 <= t < 4096 for o in out for t in o["token_ids"])
     finally:
         llm.exit()
+
+
+def _microbatch_runner_worker(rank, world, port, model_dir, results):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "tests"), os.path.join(root, "tests", "golden")]
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", f"tcp://127.0.0.1:{port}", world_size=world, rank=rank, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    out = {}
+    try:
+        from test_tuning_gpu import _greedy_decode
+
+        from kavor_b200 import _lib
+        from kavor_b200.config import Config
+        from kavor_b200.engine.model_runner import ModelRunner
+
+        for eager in (True, False):
+            cfg = Config(model_dir, load_format="dummy", seed=3, tensor_parallel_size=world, max_model_len=2048,
+                         max_num_seqs=4, max_num_batched_tokens=2048, num_kvcache_blocks=64,
+                         graph_batch_sizes=(4,), enforce_eager=eager, decode_microbatches=2,
+                         decode_microbatch_min_bs=2)
+            runner = ModelRunner(cfg, rank, None)
+            try:
+                assert runner.decode_microbatches is not None
+                out["eager" if eager else "graph"] = _greedy_decode(runner, False)
+            finally:
+                runner.exit()
+        out["device_error"] = _lib.device_error(clear=True)
+    except Exception as e:
+        out["error"] = repr(e)
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    results[rank] = out
+
+
+@pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")
+def test_microbatched_decode_graph_tp2(tmp_path):
+    """ModelRunner at TP=2 with Config.decode_microbatches=2: the decode step
+    (4 sequences, halves of 2) captured in a CUDA graph with the second stream
+    forked and joined inside the capture gives the tokens of the same step run
+    eagerly, on both ranks, with no device error bit (no peer wait gave up)."""
+    import torch.multiprocessing as mp
+
+    from kavor_b200.config import write_model_dir
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs 2 GPUs")
+    d = write_model_dir(str(tmp_path / "m"), "Qwen3-0.6B", num_hidden_layers=2, vocab_size=4096,
+                        max_position_embeddings=4096)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _port()
+        ps = [ctx.Process(target=_microbatch_runner_worker, args=(r, WORLD, port, d, results)) for r in range(WORLD)]
+        for p in ps:
+            p.start()
+        for p in ps:
+            p.join(timeout=600)
+        for p in ps:
+            if p.is_alive():
+                p.kill()
+        res = dict(results)
+    assert all("error" not in res[r] for r in range(WORLD)), res
+    assert all(res[r]["device_error"] == 0 for r in range(WORLD)), res
+    assert res[0]["graph"] == res[0]["eager"]
+    assert res[1]["graph"] == res[0]["graph"]

@@ -36,6 +36,8 @@ def main(argv=None) -> int:
     ap.add_argument("--async-decode", action="store_true", help="one decode step in flight (Config.async_decode)")
     ap.add_argument("--gemm", choices=["cublas", "tcgen05", "tcgen05_pair"], default="cublas")
     ap.add_argument("--pdl", action="store_true")
+    ap.add_argument("--microbatches", type=int, choices=[1, 2], default=1,
+                    help="TP > 1: decode as two halves on two streams (Config.decode_microbatches)")
     a = ap.parse_args(argv)
 
     from kavor_b200 import LLM, SamplingParams
@@ -47,7 +49,8 @@ def main(argv=None) -> int:
               for _ in range(a.num_seqs)]
     model_dir = write_model_dir(os.path.join(tempfile.mkdtemp(prefix="kvb_gen_"), "m"), a.model)
     llm = LLM(model_dir, load_format="dummy", tensor_parallel_size=a.tp, max_model_len=4096,
-              enable_prefix_caching=False, async_decode=a.async_decode, gemm_backend=a.gemm, pdl=a.pdl)
+              enable_prefix_caching=False, async_decode=a.async_decode, gemm_backend=a.gemm, pdl=a.pdl,
+              decode_microbatches=a.microbatches)
     try:
         llm.generate([[1, 2, 3, 4]], SamplingParams(max_tokens=8), use_tqdm=False)
         t0 = time.perf_counter()
@@ -59,6 +62,7 @@ def main(argv=None) -> int:
     generated = sum(len(o["token_ids"]) for o in out)
     print(json.dumps({"workload": f"offline generate, {a.model}, {a.num_seqs} seqs, prompt/output U[100,1024]",
                       "tp": a.tp, "async_decode": a.async_decode, "gemm": a.gemm, "pdl": a.pdl,
+                      "decode_microbatches": a.microbatches,
                       "total_tokens": total, "generated_tokens": generated, "seconds": dt,
                       "tok_s": total / dt, "reference_published_tok_s": REFERENCE_PUBLISHED_TOK_S,
                       "reference_hardware": "RTX 4070 Laptop 8 GB (README.md:44-55)"}), flush=True)

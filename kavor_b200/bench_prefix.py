@@ -42,6 +42,8 @@ def main(argv=None) -> int:
     ap.add_argument("--async-decode", action="store_true")
     ap.add_argument("--gemm", choices=["cublas", "tcgen05", "tcgen05_pair"], default="cublas")
     ap.add_argument("--pdl", action="store_true")
+    ap.add_argument("--microbatches", type=int, choices=[1, 2], default=1,
+                    help="TP > 1: decode as two halves on two streams (Config.decode_microbatches)")
     a = ap.parse_args(argv)
 
     from kavor_b200 import LLM, SamplingParams
@@ -52,7 +54,8 @@ def main(argv=None) -> int:
     max_len = a.prefix_len + a.suffix_max + a.max_tokens
     model_dir = write_model_dir(os.path.join(tempfile.mkdtemp(prefix="kvb_prefix_"), "m"), a.model)
     llm = LLM(model_dir, load_format="dummy", tensor_parallel_size=a.tp, max_model_len=max_len,
-              enable_prefix_caching=True, async_decode=a.async_decode, gemm_backend=a.gemm, pdl=a.pdl)
+              enable_prefix_caching=True, async_decode=a.async_decode, gemm_backend=a.gemm, pdl=a.pdl,
+              decode_microbatches=a.microbatches)
     try:
         llm.generate(prompts[:1], params, use_tqdm=False)  # the shared prefix's blocks enter the cache
         bm = llm.scheduler.block_manager
@@ -67,7 +70,7 @@ def main(argv=None) -> int:
     print(json.dumps({"workload": f"shared-prefix generate, {a.model}, TP={a.tp}, {a.num_seqs - 1} timed seqs, "
                                   f"prefix {a.prefix_len}, suffix U[{a.suffix_min},{a.suffix_max}], "
                                   f"{a.max_tokens} output tokens", "async_decode": a.async_decode, "gemm": a.gemm,
-                      "pdl": a.pdl, "prompt_tokens": prompt_tokens, "prefix_cache_hit_tokens": hits,
+                      "pdl": a.pdl, "decode_microbatches": a.microbatches, "prompt_tokens": prompt_tokens, "prefix_cache_hit_tokens": hits,
                       "generated_tokens": generated, "seconds": dt, "prompt_tok_s": prompt_tokens / dt,
                       "output_tok_s": generated / dt}), flush=True)
     return 0 if generated == (a.num_seqs - 1) * a.max_tokens else 1

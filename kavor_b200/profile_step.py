@@ -29,6 +29,8 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--context", type=int, default=1024)
     ap.add_argument("--replays", type=int, default=5)
+    ap.add_argument("--microbatches", type=int, choices=[1, 2], default=1,
+                    help="TP > 1: decode as two halves on two streams (Config.decode_microbatches)")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -59,7 +61,8 @@ def main(argv=None) -> int:
     model_dir = write_model_dir(os.path.join(tempfile.mkdtemp(prefix="kvb_prof_"), f"r{rank}"), a.model)
     cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world,
                  max_model_len=(blocks_per_seq + 1) * 256, max_num_seqs=B, max_num_batched_tokens=4096,
-                 num_kvcache_blocks=B * blocks_per_seq + 8, rdzv_port=1, graph_batch_sizes=(B,))
+                 num_kvcache_blocks=B * blocks_per_seq + 8, rdzv_port=1, graph_batch_sizes=(B,),
+                 decode_microbatches=a.microbatches)
     runner = ModelRunner(cfg, rank, None)
     Sequence.block_size = 256
     bm = BlockManager(cfg.num_kvcache_blocks, 256, enable_prefix_cache=False)

@@ -116,13 +116,26 @@ def decode_batch(batch: int, lo: int, hi: int, block_size: int, seed: int, spare
 
 def config1_layer_case(seed: int = 0) -> dict:
     """The one-layer case: one Qwen3-0.6B decoder layer, one decode step, B = 16."""
-    shape = QWEN3_06B
+    return decode_layer_case(QWEN3_06B, 16, 100, 1024, seed)
+
+
+def config3_layer_case(seed: int = 0) -> dict:
+    """One Qwen3-8B decoder layer (the headline model's shapes: hidden 4096,
+    32 q / 8 kv heads, intermediate 12288), one decode step of 8 sequences at
+    the decode-scaling case's fixed 1024-token context."""
+    return decode_layer_case(QWEN3_8B, 8, 1024, 1024, seed)
+
+
+def decode_layer_case(shape: dict, batch: int, lo: int, hi: int, seed: int) -> dict:
+    """One decoder layer of `shape` (weights from the dummy loader), one decode
+    step of `batch` sequences with contexts U[lo, hi]: hidden and residual
+    rows N(0, 1), KV pages N(0, 1)."""
     hd, hkv = shape["head_dim"], shape["num_key_value_heads"]
-    ctx, tables, nblk, pos, slots = decode_batch(16, 100, 1024, 256, seed)
+    ctx, tables, nblk, pos, slots = decode_batch(batch, lo, hi, 256, seed)
     pool, k_cache, v_cache = paged_pool(nblk, 256, hkv, hd, seed + 2)
     g = torch.Generator().manual_seed(seed + 3)
-    hidden = torch.randn(16, shape["hidden_size"], generator=g).to(torch.bfloat16)
-    residual = torch.randn(16, shape["hidden_size"], generator=g).to(torch.bfloat16)
+    hidden = torch.randn(batch, shape["hidden_size"], generator=g).to(torch.bfloat16)
+    residual = torch.randn(batch, shape["hidden_size"], generator=g).to(torch.bfloat16)
     ckpt = checkpoint(shape, seed, layers=1)
     layer = {k[len("model.layers.0."):]: v for k, v in ckpt.items() if k.startswith("model.layers.0.")}
     return dict(shape=shape, layer=layer, hidden=hidden, residual=residual, pool=pool, k_cache=k_cache,

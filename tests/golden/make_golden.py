@@ -10,7 +10,9 @@ What runs is the reference's own code on the CPU:
   (layernorm.py:330-335, :367-372; forced by lowering _MAX_FUSED_COLS);
 * RotaryEmbedding's cos_sin_cache (rotary_embedding.py:96-102) and the eager
   apply_rotary_emb / apply_rotary_emb_interleaved (:56-79);
-* SiluAndMul with torch.compile disabled (activation.py:8-11, eager);
+* SiluAndMul with torch.compile disabled (activation.py:8-11, eager); for the
+  Qwen3-8B layer case, its compiled numerics instead (fp32, one rounding:
+  what torch.compile's fused kernel computes on the GPU);
 * Qwen3DecoderLayer (qwen3.py:123-162) and Qwen3ForCausalLM (:189-219) with
   the reference's TP layers and weight loaders on a 1-rank gloo group. Its
   three non-CPU kernels are replaced: the Triton RoPE by the eager function
@@ -27,7 +29,7 @@ What runs is the reference's own code on the CPU:
   first prompt's full block prefills only its new tokens against the paged
   cache, then both decode.
 
-Outputs: ops_golden.pt, layer_golden.pt, tiny_model_golden.pt, tiny_model_golden_32.pt,
+Outputs: ops_golden.pt, layer_golden.pt, layer_8b_golden.pt, tiny_model_golden.pt, tiny_model_golden_32.pt,
 mistral_tiny_golden.pt, ernie4_5_tiny_golden.pt, prefix_cache_golden.pt, host_trace.json.
 """
 from __future__ import annotations
@@ -153,10 +155,33 @@ def _load_layer(layer, tensors: dict):
             p.data.copy_(t) if loader is None else loader(p, t)
 
 
-def golden_layer() -> dict:
+def _compiled_silu_and_mul(self, x):
+    """activation.py:8-11 as the reference runs it on the GPU: torch.compile
+    fuses silu(x) * y into one kernel that computes in fp32 and rounds once.
+    Its eager form (what runs on the CPU with compilation disabled) rounds
+    silu(x) to bf16 first; over the 12288 intermediate features of a Qwen3-8B
+    MLP those extra roundings move the down projection's outputs by more than
+    the per-layer bound, so the 8B layer case uses the compiled numerics."""
+    g, u = x.float().chunk(2, -1)
+    return (torch.nn.functional.silu(g) * u).to(x.dtype)
+
+
+def golden_layer(case_fn=cases.config1_layer_case, compiled_silu: bool = False) -> dict:
+    from kavor.layers.activation import SiluAndMul
+
+    case = case_fn(0)
+    eager_forward = SiluAndMul.forward
+    if compiled_silu:
+        SiluAndMul.forward = _compiled_silu_and_mul
+    try:
+        return _run_layer_case(case)
+    finally:
+        SiluAndMul.forward = eager_forward
+
+
+def _run_layer_case(case) -> dict:
     from kavor.utils.context import reset_context, set_context
 
-    case = cases.config1_layer_case(0)
     layer = _ref_layer(cases.hf_config(case["shape"]))
     _load_layer(layer, case["layer"])
     attn = layer.self_attn.attn
@@ -394,6 +419,7 @@ def main() -> int:
     out = Path(args.out)
     torch.save(golden_ops(), out / "ops_golden.pt")
     torch.save(golden_layer(), out / "layer_golden.pt")
+    torch.save(golden_layer(cases.config3_layer_case, compiled_silu=True), out / "layer_8b_golden.pt")
     torch.save(golden_tiny_model(), out / "tiny_model_golden.pt")
     torch.save(golden_tiny_model(decode_steps=31, keep_logits=False), out / "tiny_model_golden_32.pt")
     for family in cases.FAMILIES:

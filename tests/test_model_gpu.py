@@ -39,11 +39,23 @@ def _load(module, tensors, packed):
 def test_config1_decoder_layer_matches_reference():
     """One Qwen3-0.6B layer, one decode step, B=16, vs the reference layer's
     output: max-abs 2e-2 / rel 1e-2 (the per-layer parity bound)."""
+    _replay_layer_golden(cases.config1_layer_case(0), "layer_golden.pt")
+
+
+@pytest.mark.skipif(__import__("os").environ.get("KVB_GPU_PENDING") != "1",
+                    reason="first GPU run pending (KVB_GPU_PENDING=1)")
+def test_8b_decoder_layer_matches_reference():
+    """One Qwen3-8B layer (the headline model's shapes), one decode step of 8
+    sequences at context 1024, vs the reference layer's output under the same
+    per-layer bound."""
+    _replay_layer_golden(cases.config3_layer_case(0), "layer_8b_golden.pt")
+
+
+def _replay_layer_golden(case, fixture):
     from kavor_b200.models.qwen3 import Qwen3DecoderLayer, Qwen3ForCausalLM
     from kavor_b200.utils.context import reset_context, set_context
 
-    case = cases.config1_layer_case(0)
-    gold = torch.load(GOLDEN / "layer_golden.pt", weights_only=False)
+    gold = torch.load(GOLDEN / fixture, weights_only=False)
     layer = _build(lambda: Qwen3DecoderLayer(cases.hf_config(case["shape"])))
     _load(layer, case["layer"], Qwen3ForCausalLM.packed_modules_mapping)
     for variant, res in (("first", None), ("later", case["residual"])):

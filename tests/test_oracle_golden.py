@@ -60,7 +60,9 @@ def test_silu_mul_within_one_rounding_of_reference_eager():
 
 
 def _oracle_layer(case, residual):
-    shape = omodel.Shape(hidden=1024, inter=3072, layers=1, hq=16, hkv=8)
+    sh = case["shape"]
+    shape = omodel.Shape(hidden=sh["hidden_size"], inter=sh["intermediate_size"], layers=1,
+                         hq=sh["num_attention_heads"], hkv=sh["num_key_value_heads"])
     p = {"model.layers.0." + k: v for k, v in case["layer"].items()}
     pool = case["pool"].clone()
     batch = omodel.Batch(False, case["positions"], case["slot_mapping"], context_lens=case["context_lens"],
@@ -73,6 +75,17 @@ def test_decoder_layer_matches_reference_layer():
     """The one-layer case: one 0.6B decoder layer, one decode step, B=16."""
     case = cases.config1_layer_case(0)
     gold = _load("layer_golden.pt")
+    for variant, res in (("first", None), ("later", case["residual"].clone())):
+        h, r = _oracle_layer(case, res)
+        torch.testing.assert_close(r.float(), gold[variant]["residual"].float(), atol=2e-2, rtol=1e-2)
+        torch.testing.assert_close(h.float(), gold[variant]["hidden"].float(), atol=2e-2, rtol=1e-2)
+
+
+def test_8b_decoder_layer_matches_reference_layer():
+    """One Qwen3-8B decoder layer (hidden 4096, 32 q / 8 kv heads,
+    intermediate 12288), one decode step of 8 sequences at context 1024."""
+    case = cases.config3_layer_case(0)
+    gold = _load("layer_8b_golden.pt")
     for variant, res in (("first", None), ("later", case["residual"].clone())):
         h, r = _oracle_layer(case, res)
         torch.testing.assert_close(r.float(), gold[variant]["residual"].float(), atol=2e-2, rtol=1e-2)

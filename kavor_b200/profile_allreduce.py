@@ -12,6 +12,11 @@ an NVLink multicast mapping), against the reference's sequence: NCCL
 w ~ N(1, 0.1), eps 1e-6; consecutive calls alternate two partial buffers, as
 the layers of a forward do. Prints one JSON line per case on rank 0 with the
 average call time and the bus bandwidth 2 (N-1)/N T H 2 bytes / time.
+
+``--halves``: also times the decode micro-batch form (Config.decode_microbatches
+= 2): two communicators, grids capped at DecodeMicrobatches.MAX_BLOCKS, each
+reducing half of the T rows, the second on another stream, both in flight
+together (``halves_us`` = time per pair of half calls).
 """
 from __future__ import annotations
 
@@ -25,7 +30,7 @@ import torch.distributed as dist
 
 from kavor_b200 import _kernels as K
 from kavor_b200 import _lib
-from kavor_b200.layers.allreduce import TPAllReduce
+from kavor_b200.layers.allreduce import DecodeMicrobatches, TPAllReduce
 
 
 def _time_graph(fn, iters: int, warmup: int) -> float:
@@ -64,6 +69,7 @@ def main(argv=None) -> int:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--backend", default="auto", choices=["auto", "symmetric", "ipc"])
+    ap.add_argument("--halves", action="store_true", help="also time two half-size calls in flight together")
     a = ap.parse_args(argv)
     hiddens = [int(x) for x in a.hidden.split(",")]
     tokens = [int(x) for x in a.tokens.split(",")]
@@ -76,6 +82,17 @@ def main(argv=None) -> int:
     for H in hiddens:
         tmax = max(tokens)
         ar = TPAllReduce(tmax, H, dev, backend=a.backend)
+        halves = None
+        if a.halves:  # the decode micro-batches' communicators and per-half rows
+            hmax = (tmax + 1) // 2
+            halves = [TPAllReduce(hmax, H, dev, backend=a.backend, max_blocks=DecodeMicrobatches.MAX_BLOCKS)
+                      for _ in range(2)]
+            for c in halves:
+                for i in range(2):
+                    c.buffers[i].copy_(torch.randn(hmax, H, device=dev, generator=g).to(torch.bfloat16))
+            half_res = [torch.randn(hmax, H, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+            half_out = [torch.empty(hmax, H, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+            side = torch.cuda.Stream(dev)
         modes = (("fused_auto", 0), ("fused_one_shot", 1), ("fused_two_shot", 2))
         if ar.multicast:
             modes += (("fused_switch_one_shot", 3), ("fused_switch_two_shot", 4))
@@ -99,6 +116,20 @@ def main(argv=None) -> int:
                 t = _time_graph(fused(mode), a.iters, a.warmup)
                 row[name + "_us"] = t * 1e6
 
+            if halves is not None and T >= 2:
+                def pair(i):
+                    main = torch.cuda.current_stream()
+                    side.wait_stream(main)
+                    for m, n in enumerate((T - T // 2, T // 2)):
+                        st = main if m == 0 else side
+                        with torch.cuda.stream(st):
+                            _lib.call("kvb_allreduce_add_rmsnorm", halves[m].comm, i & 1, half_res[m].data_ptr(),
+                                      half_res[m].data_ptr(), half_out[m].data_ptr(), w.data_ptr(), n, H, 1e-6, 0,
+                                      st.cuda_stream)
+                    main.wait_stream(side)
+
+                row["halves_us"] = _time_graph(pair, a.iters, a.warmup) * 1e6
+
             def nccl(i):
                 x = nccl_x[i & 1][:T]
                 dist.all_reduce(x)
@@ -112,6 +143,9 @@ def main(argv=None) -> int:
             if rank == 0:
                 print(json.dumps(row), flush=True)
         del nccl_x, res, out
+        if halves is not None:
+            for c in halves:
+                c.close()
         ar.close()
     dist.barrier()
     dist.destroy_process_group()

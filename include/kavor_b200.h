@@ -280,10 +280,11 @@ int kvb_comm_attach(int rank, int world, const uint64_t* peer_bases, uint64_t mu
                     size_t max_bytes, void** comm);
 /* Largest grid (blocks) of this communicator's kvb_allreduce_add_rmsnorm
  * launches, 1..256 (default 256; a block then handles several rows). Every
- * rank of the group must set the same value. Each block of a call waits for
- * the same block of every peer, so all blocks of a call must be resident at
- * once: a caller that runs two groups' calls concurrently on two streams caps
- * both, so that the two grids together leave SMs free for the other kernels.
+ * rank of the group must set the same value. Each block of a call spins,
+ * holding its SM slot, until the same block has arrived on every peer: a
+ * caller that runs two groups' calls concurrently on two streams caps both,
+ * so that the two grids together leave SMs free for the kernels the peers
+ * wait behind.
  * No reference counterpart (the reference issues one NCCL all-reduce at a
  * time, linear.py:158-159). */
 int kvb_comm_set_max_blocks(void* comm, int max_blocks);

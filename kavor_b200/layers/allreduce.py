@@ -188,13 +188,15 @@ class DecodeMicrobatches:
     HBM bandwidth, runs beside the other half's GEMMs and all-reduces, which
     are bound by latency at decode sizes.
 
-    Every block of an all-reduce call waits for the same block on every peer,
-    so a call must have all its blocks resident at once; the two halves' calls
-    can be in flight together, so both communicators cap their grids
-    (``max_blocks``) to leave SMs for the other kernels.
+    Every block of an all-reduce call spins, holding its SM slot, until the
+    same block has arrived on every peer. With both halves' calls in flight,
+    uncapped grids could hold a slot on every SM and leave no room for a
+    kernel that needs a whole SM and that a peer's call waits behind; both
+    communicators therefore cap their grids (``max_blocks``) so that SMs stay
+    free for the other kernels.
 
-    ``streams``: None runs both halves on the current stream (no CUDA: the
-    CPU tests of the wiring), else the second half's stream."""
+    ``side_stream``: the second half's stream; None runs both halves on the
+    current stream (no CUDA: the CPU tests of the wiring)."""
 
     MAX_BLOCKS = 64
 

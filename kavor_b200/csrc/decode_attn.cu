@@ -20,6 +20,8 @@
 // raises the device error bit and the tile is read as zeros (TMA OOB fill).
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "../../include/kavor_b200.h"
 
@@ -461,20 +463,27 @@ namespace kvb {
 namespace {
 
 // Device address of the built-in area for the current device. The lookup runs
-// once per device, on the first call made while that device is current.
+// once per device, on the first call made while that device is current (it
+// may load the module, which is why that first call belongs before any stream
+// capture). The cached address belongs to the device's primary context: a
+// process that resets the device (cudaDeviceReset) must not call this entry
+// point again. Host threads may race on the first lookup; each stores the same
+// address, and the slots are atomic.
 int static_scratch_address(float** out) {
-  static float* addr[64] = {};
+  static std::atomic<float*> addr[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return set_error(kUnsupported, "kvb_paged_decode_attn_no_alloc: device index >= 64");
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+  float* p = addr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* sym = nullptr;
+    e = cudaGetSymbolAddress(&sym, g_decode_static_scratch);
     if (e != cudaSuccess) return cuda_status(e, "kvb_paged_decode_attn_no_alloc: cudaGetSymbolAddress");
-    addr[dev] = static_cast<float*>(p);
+    p = static_cast<float*>(sym);
+    addr[dev].store(p, std::memory_order_release);
   }
-  *out = addr[dev];
+  *out = p;
   return kOk;
 }
 

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import atexit
 import logging
+import signal
 from dataclasses import fields
 from time import monotonic, perf_counter
 
@@ -27,11 +28,20 @@ from kavor_b200.sampling_params import SamplingParams
 
 logger = logging.getLogger("kavor_b200")
 
-WORKER_EXIT_TIMEOUT = 10.0
-WORKER_KILL_TIMEOUT = 5.0
+WORKER_EXIT_TIMEOUT = 10.0   # after the exit message
+WORKER_STOP_TIMEOUT = 330.0  # after a stop request (covers the process group's 300 s timeout)
+
+
+def _stop_requested(signum, frame):
+    raise SystemExit(f"TP worker stopped by signal {signum}")
 
 
 def _worker_entry(config: Config, rank: int, event) -> None:
+    # SIGTERM (LLMEngine._reap's stop request, or multiprocessing's exit
+    # handling of daemonic children) becomes SystemExit in the worker's main
+    # thread: ModelRunner.loop unwinds through abandon(), which closes the
+    # all-reduce areas with the other ranks before the process ends
+    signal.signal(signal.SIGTERM, _stop_requested)
     ModelRunner(config, rank, event)
 
 
@@ -54,6 +64,11 @@ class LLMEngine:
         self.ps = []
         self.events = []
         self._exiting = False
+        # whether a worker that ignores a stop request may be killed: only when
+        # no rank holds memory that may be bound to an NVLink multicast object
+        # (ending such a rank can fault the other ranks' GPUs); unknown until
+        # rank 0's runner has chosen its all-reduce backend
+        self._kill_ok = config.tensor_parallel_size == 1
         self.step_stats: list[dict] = []
         self.request_stats: list[dict] = []
         ctx = mp.get_context("spawn")
@@ -66,6 +81,8 @@ class LLMEngine:
         atexit.register(self.exit)
         try:
             self.model_runner = ModelRunner(config, 0, self.events)
+            tp = self.model_runner.tp_allreduce
+            self._kill_ok = tp is None or tp.backend == "ipc"
             self.tokenizer = _load_tokenizer(config.model, config.trust_remote_code)
             if self.tokenizer is not None and self.tokenizer.eos_token_id is not None:
                 config.eos = self.tokenizer.eos_token_id
@@ -93,22 +110,32 @@ class LLMEngine:
             self._reap(graceful=False)
 
     def _reap(self, graceful: bool) -> None:
+        """Wait for the workers; a worker still running gets SIGTERM, which
+        its entry turns into an orderly exit (communicator closed with the
+        other ranks). A worker that does not stop is killed only when no rank
+        holds multicast-bound memory; otherwise it is logged and left alone."""
         if graceful:
             deadline = monotonic() + WORKER_EXIT_TIMEOUT
             for p in self.ps:
                 p.join(timeout=max(0.0, deadline - monotonic()))
         for p in self.ps:
             if p.is_alive():
-                logger.warning("TP worker %s did not exit, sending SIGTERM", p.name)
+                logger.warning("TP worker %s did not exit, asking it to stop", p.name)
                 p.terminate()
-        deadline = monotonic() + WORKER_KILL_TIMEOUT
+        deadline = monotonic() + WORKER_STOP_TIMEOUT
         for p in self.ps:
             p.join(timeout=max(0.0, deadline - monotonic()))
         for p in self.ps:
-            if p.is_alive():
-                logger.warning("TP worker %s ignored SIGTERM, sending SIGKILL", p.name)
+            if not p.is_alive():
+                continue
+            if self._kill_ok:
+                logger.warning("TP worker %s ignored the stop request, killing it", p.name)
                 p.kill()
                 p.join(timeout=2.0)
+            else:
+                logger.error("TP worker %s ignored the stop request; left running: its all-reduce area may be "
+                             "bound to an NVLink multicast object, and ending it could fault the other GPUs",
+                             p.name)
 
     def add_request(self, prompt, sampling_params: SamplingParams, request_id: str | None = None) -> int:
         if isinstance(prompt, str):

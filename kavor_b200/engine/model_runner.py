@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import datetime
 import itertools
+import multiprocessing
 import os
 import pickle
 import time
@@ -39,6 +40,7 @@ from kavor_b200.utils.context import reset_context, set_context
 
 SHM_BYTES = 1 << 22
 MAILBOX_WAIT_S = 60.0  # rank 0 waits at most this long for every worker to take the previous message
+MAILBOX_POLL_S = 1.0   # a worker checks that rank 0's process is still alive this often while idle
 
 
 # ----------------------------------------------------------------- host metadata
@@ -334,14 +336,24 @@ class ModelRunner:
             self.loop()
 
     def loop(self) -> None:
-        while True:
-            method, args = self.read_shm()
-            self.call(method, *args)
-            if method == "exit":
-                break
+        try:
+            while True:
+                method, args = self.read_shm()
+                self.call(method, *args)
+                if method == "exit":
+                    break
+        except BaseException:
+            # a stop request (SIGTERM turned into SystemExit by the engine's
+            # worker entry), rank 0 gone, or a failed call: release this
+            # rank's areas in order instead of leaving them to process exit
+            self.abandon()
+            raise
 
     def read_shm(self):
-        self.event.wait()
+        parent = multiprocessing.parent_process()
+        while not self.event.wait(MAILBOX_POLL_S):
+            if parent is not None and not parent.is_alive():
+                raise SystemExit(f"TP worker {self.rank}: rank 0's process exited without sending exit")
         n = int.from_bytes(self.shm.buf[0:4], "little")
         method, *args = pickle.loads(self.shm.buf[4:n + 4])
         self.event.clear()
@@ -396,6 +408,32 @@ class ModelRunner:
             set_tp_allreduce(None)
             self.tp_allreduce.close()
             self.tp_allreduce = None
+        if self.owns_process_group and dist.is_initialized():
+            dist.destroy_process_group()
+
+    def abandon(self) -> None:
+        """Leave without the exit message (a worker that was asked to stop, or
+        whose rank 0 is gone): no mailbox barrier; the device is drained and
+        the all-reduce areas are closed (collectively: the other ranks' kernels
+        may still read this rank's buffers, and the process-group timeout
+        bounds the wait for a rank that is gone) before the process group is
+        destroyed, so no area that may be bound to an NVLink multicast object
+        disappears under a peer that is still using it."""
+        if self.shm is not None:
+            self.shm.close()
+            self.shm = None
+        self.graphs.clear()
+        self.graph_pool = None
+        try:
+            torch.cuda.synchronize()
+            for comm in (self.decode_microbatches, self.tp_allreduce):
+                if comm is not None:
+                    comm.close()
+        except Exception:  # noqa: BLE001 - a peer is gone: the barrier timed out
+            pass
+        self.decode_microbatches = self.tp_allreduce = None
+        set_decode_microbatches(None)
+        set_tp_allreduce(None)
         if self.owns_process_group and dist.is_initialized():
             dist.destroy_process_group()
 

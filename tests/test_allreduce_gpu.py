@@ -15,6 +15,7 @@ import socket
 
 import pytest
 import torch
+from rank_procs import check_stop, run_ranks
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +44,7 @@ def _expected(T, salt, residual, weight, world):
     return ops.add_rmsnorm(y, residual, weight, 1e-6)
 
 
-def _worker(rank, world, port, results, backend):
+def _worker(rank, world, port, backend, results, stop):
     import datetime
     import sys
 
@@ -69,6 +70,7 @@ def _worker(rank, world, port, results, backend):
         for mode in modes:
             for T in (1, 7, 256, 1000):
                 for with_res in (False, True):
+                    check_stop(stop)
                     salt += 1
                     res = _partial(7, T, salt) if with_res else None
                     ar.partial_buffer(idx, T).copy_(_partial(rank, T, salt).to(dev))
@@ -106,6 +108,7 @@ def _worker(rank, world, port, results, backend):
             bufs[0].copy_(o1)
             o2, r2 = ar.reduce_norm(0, T, r1, dw, 1e-6)
         for rep in range(3):
+            check_stop(stop)
             salt += 1
             resid.zero_()
             bufs[2].copy_(_partial(rank, T, salt).to(dev))
@@ -148,27 +151,12 @@ def _worker(rank, world, port, results, backend):
 
 @pytest.mark.parametrize("backend,world", [("ipc", 2), ("symmetric", 2), ("symmetric", 4), ("symmetric", 8)])
 def test_fused_allreduce(backend, world):
-    import torch.multiprocessing as mp
-
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     if backend == "ipc":
         os.environ["NCCL_NVLS_ENABLE"] = "0"
     else:
         os.environ.pop("NCCL_NVLS_ENABLE", None)
-    ctx = mp.get_context("spawn")
-    with ctx.Manager() as m:
-        results = m.dict()
-        port = _port()
-        procs = [ctx.Process(target=_worker, args=(r, world, port, results, backend)) for r in range(world)]
-        for p in procs:
-            p.start()
-        for p in procs:
-            p.join(timeout=300)
-        for p in procs:
-            if p.is_alive():
-                p.kill()
-        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-        res = dict(results)
-        assert [res[r][0] for r in range(world)] == [[]] * world, res
-        assert res[0][1].startswith(backend), res
+    res = run_ranks(_worker, world, (_port(), backend), timeout=300)
+    assert [res[r][0] for r in range(world)] == [[]] * world, res
+    assert res[0][1].startswith(backend), res

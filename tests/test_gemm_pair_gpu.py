@@ -1,18 +1,11 @@
 """CTA-pair GEMM (kvb_gemm_pair_bf16, tcgen05 cta_group::2) against an fp32
 reference and cuBLAS over decode and prefill shapes of the Qwen3 projections,
-ragged M and N, forced K splits, NaN-filled outputs and determinism.
-
-The kernel has not run on a GPU yet: these tests run only with
-KVB_GPU_PENDING=1 until their first run on a B200 has passed."""
-import os
-
+ragged M and N, forced K splits, NaN-filled outputs and determinism."""
 import pytest
 import torch
 import torch.nn.functional as F
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("KVB_GPU_PENDING") != "1",
-                                 reason="first GPU run of the CTA-pair GEMM pending (KVB_GPU_PENDING=1)")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

@@ -11,6 +11,7 @@ import socket
 
 import pytest
 import torch
+from rank_procs import check_stop, run_ranks
 
 pytestmark = pytest.mark.gpu
 WORLD = 2  # LLM.generate test
@@ -24,7 +25,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, results, microbatch=False):
+def _worker(rank, world, port, microbatch, results, stop):
     import datetime
     import sys
 
@@ -81,6 +82,7 @@ def _worker(rank, world, port, results, microbatch=False):
             cu = torch.tensor([0] + torch.tensor([len(s) for s in seqs]).cumsum(0).tolist(), **i32)
             slots = torch.tensor([tables[b][0] * 256 + i for b, s in enumerate(seqs) for i in range(len(s))], **i32)
             for step in range(5):
+                check_stop(stop)
                 # ranks start each forward together (the fused all-reduce's peer wait
                 # is bounded at about a second; host work between steps is not)
                 torch.cuda.synchronize()
@@ -119,37 +121,18 @@ def _worker(rank, world, port, results, microbatch=False):
     results[rank] = out
 
 
-PENDING = os.environ.get("KVB_GPU_PENDING") != "1"
-
-
 @pytest.mark.parametrize("world,microbatch", [
     (2, False), (4, False), (8, False),
-    # decode steps split into two micro-batches on two streams: not yet run on
-    # a GPU, so only with KVB_GPU_PENDING=1 until its first run has passed
-    pytest.param(2, True, marks=pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")),
-    pytest.param(8, True, marks=pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")),
+    # decode steps split into two micro-batches on two streams
+    (2, True), (8, True),
 ])
 def test_tp_model_matches_oracle(world, microbatch):
-    import torch.multiprocessing as mp
-
     import cases
     from oracle import model as omodel
 
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    ctx = mp.get_context("spawn")
-    with ctx.Manager() as m:
-        results = m.dict()
-        port = _port()
-        ps = [ctx.Process(target=_worker, args=(r, world, port, results, microbatch)) for r in range(world)]
-        for p in ps:
-            p.start()
-        for p in ps:
-            p.join(timeout=600)
-        for p in ps:
-            if p.is_alive():
-                p.kill()
-        res = dict(results)
+    res = run_ranks(_worker, world, (_port(), microbatch), timeout=600)
     assert all("error" not in res[r] for r in range(world)), res
     assert all(res[r]["device_error"] == 0 for r in range(world)), res
     steps0 = res[0]["steps"]
@@ -206,7 +189,7 @@ def test_llm_generate_tp2(tmp_path):
         llm.exit()
 
 
-def _microbatch_runner_worker(rank, world, port, model_dir, results):
+def _microbatch_runner_worker(rank, world, port, model_dir, results, stop):
     import datetime
     import sys
 
@@ -227,6 +210,7 @@ def _microbatch_runner_worker(rank, world, port, model_dir, results):
         from kavor_b200.engine.model_runner import ModelRunner
 
         for eager in (True, False):
+            check_stop(stop)
             cfg = Config(model_dir, load_format="dummy", seed=3, tensor_parallel_size=world, max_model_len=2048,
                          max_num_seqs=4, max_num_batched_tokens=2048, num_kvcache_blocks=64,
                          graph_batch_sizes=(4,), enforce_eager=eager, decode_microbatches=2,
@@ -246,33 +230,18 @@ def _microbatch_runner_worker(rank, world, port, model_dir, results):
     results[rank] = out
 
 
-@pytest.mark.skipif(PENDING, reason="first GPU run pending (KVB_GPU_PENDING=1)")
 def test_microbatched_decode_graph_tp2(tmp_path):
     """ModelRunner at TP=2 with Config.decode_microbatches=2: the decode step
     (4 sequences, halves of 2) captured in a CUDA graph with the second stream
     forked and joined inside the capture gives the tokens of the same step run
     eagerly, on both ranks, with no device error bit (no peer wait gave up)."""
-    import torch.multiprocessing as mp
-
     from kavor_b200.config import write_model_dir
 
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip("needs 2 GPUs")
     d = write_model_dir(str(tmp_path / "m"), "Qwen3-0.6B", num_hidden_layers=2, vocab_size=4096,
                         max_position_embeddings=4096)
-    ctx = mp.get_context("spawn")
-    with ctx.Manager() as m:
-        results = m.dict()
-        port = _port()
-        ps = [ctx.Process(target=_microbatch_runner_worker, args=(r, WORLD, port, d, results)) for r in range(WORLD)]
-        for p in ps:
-            p.start()
-        for p in ps:
-            p.join(timeout=600)
-        for p in ps:
-            if p.is_alive():
-                p.kill()
-        res = dict(results)
+    res = run_ranks(_microbatch_runner_worker, WORLD, (_port(), d), timeout=600)
     assert all("error" not in res[r] for r in range(WORLD)), res
     assert all(res[r]["device_error"] == 0 for r in range(WORLD)), res
     assert res[0]["graph"] == res[0]["eager"]

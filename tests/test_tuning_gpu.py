@@ -4,18 +4,11 @@ default paths' tests: GEMM K splits whose cluster size is not a power of two
 ranks), the L2 prefetch of the weight stream (kvb_gemm_set_l2_prefetch), the
 tcgen05 GEMM backend inside the model, pipelined decode
 (ModelRunner.run_async with one step in flight, and the engine's
-DecodePipeline) and programmatic dependent launch (kvb_set_pdl).
-
-None of these options has run on a GPU yet: the tests run only with
-KVB_GPU_PENDING=1 until their first run on a B200 has passed."""
-import os
-
+DecodePipeline) and programmatic dependent launch (kvb_set_pdl)."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("KVB_GPU_PENDING") != "1",
-                                 reason="first GPU run of these off-by-default options pending (KVB_GPU_PENDING=1)")]
+pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 

@@ -38,9 +38,25 @@ def _call_no_alloc(lib, q, pool, tables, ctx, out, splits):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
 
 
+def _oracle(q, pool, tables, ctx):
+    from oracle import ops
+
+    return ops.paged_decode_attention(q.cpu(), pool[:, 0].cpu(), pool[:, 1].cpu(), tables.cpu(), ctx.cpu(),
+                                      128 ** -0.5)
+
+
+# 3 sequences x 32 query heads = 96 partial rows of 516 B (128 fp32 values and
+# a log-sum-exp) per split: 169 splits use 8,371,584 B of the 8 MiB area, 170
+# would need 8,421,120 B
+SPLITS_AT_LIMIT = 169
+
+
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
-@pytest.mark.parametrize("splits", [4, 0])
+@pytest.mark.parametrize("splits", [1, 4, 0, SPLITS_AT_LIMIT])
 def test_no_alloc_decode_matches_workspace_entry_point_twice(splits):
+    """splits 1 uses no scratch, 0 lets the library choose, 169 fills the
+    built-in area up to its last whole split; each output equals the
+    workspace entry point's within the attention tolerance, and the oracle's."""
     from kavor_b200 import _kernels as K
     from kavor_b200 import _lib
 
@@ -53,17 +69,18 @@ def test_no_alloc_decode_matches_workspace_entry_point_twice(splits):
         assert rc == 0, lib.kvb_last_error()
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float(), ref.float(), atol=2e-2, rtol=1e-2)
+        torch.testing.assert_close(out.float().cpu(), _oracle(q, pool, tables, ctx).float(), atol=2e-2, rtol=1e-2)
     assert _lib.device_error(clear=True) == 0
 
 
 @pytest.mark.skipif(not torch.cuda.is_available(), reason="needs CUDA")
-def test_no_alloc_decode_rejects_scratch_beyond_its_limit():
+@pytest.mark.parametrize("splits", [SPLITS_AT_LIMIT + 1, 2000])
+def test_no_alloc_decode_rejects_scratch_beyond_its_limit(splits):
     from kavor_b200 import _lib
 
     lib = _lib.load()
     q, pool, tables, ctx = _case(2)
     out = torch.empty_like(q)
-    # 3 sequences x 32 heads x 2000 splits x 516 B = 99 MB > 8 MiB
-    rc = _call_no_alloc(lib, q, pool, tables, ctx, out, 2000)
+    rc = _call_no_alloc(lib, q, pool, tables, ctx, out, splits)
     assert rc == -3
     assert b"built-in area" in lib.kvb_last_error()

@@ -66,6 +66,8 @@ def parse_args(argv=None):
                     help="skip the one-GPU probes of the package's GEMM in place of cuBLAS")
     ap.add_argument("--microbatches", type=int, choices=[1, 2], default=1,
                     help="TP > 1: 2 runs the decode step as two halves on two streams (Config.decode_microbatches)")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the smaller decode batches (1, 16, 64) and, at TP > 1, the all-reduce microbenchmark")
     ap.add_argument("--e2e-pipelined", action="store_true",
                     help="e2e through ModelRunner.run_async with one step in flight (host work overlaps the GPU)")
     return ap.parse_args(argv)
@@ -234,7 +236,8 @@ def run_reference(args) -> int:
     t_step = sum(steps) / len(steps)
     value = args.batch / t_step
     sample = (f"each step: 1 of {shape['num_hidden_layers']} decoder layers + the LM head of one decode step "
-              f"(B={args.batch}, ctx={args.context}) on the CPU oracle, extrapolated x{shape['num_hidden_layers']}")
+              f"(B={args.batch}, ctx={args.context}) on the CPU oracle, extrapolated x{shape['num_hidden_layers']}; "
+              f"weights and KV pages are deterministic ramp fills (the CPU time does not depend on the values)")
     line = {
         "impl": "reference", "metric": f"decode output tok/s ({args.model}, B={args.batch}, ctx={args.context})",
         "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -279,6 +282,7 @@ def allreduce_bus_bytes(shape: dict, tp: int, batch: int) -> float:
 
 
 NVLINK_GBS = 900.0  # nominal per direction per GPU (the roofline's all-reduce term)
+SWEEP_BATCHES = (1, 16, 64)  # BASELINE config 3's decode batches beside the headline 256
 
 
 def attention_bytes(batch: int, context: int, hq: int, hkv: int) -> int:
@@ -316,9 +320,10 @@ def run_ours(args) -> int:
     blocks_per_seq = (ctx0 + 2 * extra + 255) // 256
     tmp = tempfile.mkdtemp(prefix="kvb_bench_")
     model_dir = write_model_dir(os.path.join(tmp, f"r{rank}"), args.model)
+    sweep = [b for b in SWEEP_BATCHES if b < B] if not args.no_sweep else []
     cfg = Config(model_dir, load_format="dummy", seed=0, tensor_parallel_size=world, max_model_len=max_len,
                  max_num_seqs=B, max_num_batched_tokens=4096, num_kvcache_blocks=B * blocks_per_seq + 8,
-                 rdzv_port=1, graph_batch_sizes=(B,), gemm_backend=args.gemm,
+                 rdzv_port=1, graph_batch_sizes=tuple(sweep) + (B,), gemm_backend=args.gemm,
                  gemm_l2_prefetch=args.gemm_l2_prefetch, pdl=args.pdl, decode_microbatches=args.microbatches)
     runner = ModelRunner(cfg, rank, None)
     with torch.no_grad():
@@ -363,6 +368,30 @@ def run_ours(args) -> int:
     ms_per_step = t_dev / args.steps * 1e3
     value = B * args.steps / t_dev
     launches = runner.graph_launches.get(bucket, 0) * args.steps
+
+    # --- the decode-scaling batch sizes below B: the first b
+    # sequences, every one at context ctx0, each size's captured graph replayed
+    batch_sweep = {}
+    for b in sweep:
+        runner.run(seqs[:b], False)  # static inputs of bucket b
+        gb = runner.graphs[next(x for x in runner.graph_bs if x >= b)]
+        for _ in range(args.warmup):
+            gb.replay()
+        torch.cuda.synchronize()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            gb.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        barrier()
+        tb = max_over_ranks(s0.elapsed_time(s1) / 1e3)
+        roof_b = max(step_bytes(shape, world, b, ctx0) / (measured_peaks()[0] * 1e9),
+                     allreduce_bus_bytes(shape, world, b) / (NVLINK_GBS * 1e9))
+        batch_sweep[str(b)] = {"tok_s": b * args.steps / tb, "ms_per_step": tb / args.steps * 1e3,
+                               "step_roofline_frac": roof_b / (tb / args.steps)}
+    runner.run(seqs, False)  # back to the full batch
 
     # --- decode attention alone, rotating over the layers' caches (no L2 reuse)
     attn = [m for m in runner.model.modules() if hasattr(m, "k_cache") and hasattr(m, "v_cache")]
@@ -442,6 +471,14 @@ def run_ours(args) -> int:
                "api": ("ModelRunner.run_async(seqs, chain=True), one step in flight" if args.e2e_pipelined
                        else "ModelRunner.run(seqs, is_prefill=False)")}
 
+    # --- BASELINE config 5 at this TP size: the fused all-reduce + add+RMSNorm
+    # against NCCL all_reduce + add+RMSNorm, on the model's communicator
+    ar_micro = None
+    if world > 1 and runner.tp_allreduce is not None and not args.no_sweep:
+        from kavor_b200.profile_allreduce import fused_vs_nccl
+
+        ar_micro = fused_vs_nccl(runner.tp_allreduce, [1, 16, 256, 4096])
+
     dev_err = _lib.device_error(clear=True)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -451,7 +488,8 @@ def run_ours(args) -> int:
         cpu = {"value": B / t_step, "unit": "tok/s", "cores": threads, "kind": "port",
                "sample": f"5 sampled decode steps (B={B}, ctx={ctx0}): each 1 timed decoder layer of "
                          f"{shape['num_hidden_layers']} + 1 LM-head GEMM on the CPU oracle, extrapolated "
-                         f"x{shape['num_hidden_layers']}",
+                         f"x{shape['num_hidden_layers']}; weights and KV pages are deterministic ramp fills "
+                         f"(the CPU time does not depend on the values)",
                "ms_per_step": t_step * 1e3}
 
     # the pipelined e2e beside the synchronous one (one GPU, no collectives; a failure is reported, not raised)
@@ -475,6 +513,10 @@ def run_ours(args) -> int:
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches, "device_error_bits": dev_err,
         }
+        if batch_sweep:
+            line["batch_sweep"] = batch_sweep
+        if ar_micro is not None:
+            line["allreduce_add_rmsnorm_microbench"] = ar_micro
         if e2e_pipelined is not None:
             line["e2e_pipelined"] = e2e_pipelined
         if gemm_probes is not None:

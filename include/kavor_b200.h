@@ -244,6 +244,31 @@ int kvb_gemm_pair_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t l
  * plan[3] CTAs. */
 int kvb_gemm_pair_plan(int M, int N, int K, int splits, int gated, int* plan);
 
+/* Decode-batch GEMM (the F.linear of linear.py:50,73,157 and embed_head.py:61
+ * at M <= 256 tokens; larger M works, tiled by 256 tokens): y[M, N] =
+ * x[M, K] * w[N, K]^T on CTA pairs (tcgen05 cta_group::2, 256 weight rows x up
+ * to 256 tokens per MMA) with a stream-K schedule: one wave of persistent
+ * pairs shares the (tile, K-step) iterations equally; a tile cut between
+ * pairs is summed by its first segment from fp32 partials the others leave in
+ * `workspace`, in K order (deterministic). Operand rules as kvb_gemm_bf16.
+ * `workspace` (256-byte aligned, at least kvb_gemm_sk_workspace_size bytes)
+ * must be zero when first used; the kernel leaves it zero again after every
+ * normal launch (after a device error bit it must be zeroed again). Launches
+ * that share a workspace must be ordered on one stream. */
+int kvb_gemm_sk_workspace_size(int M, int N, int K, int gated, size_t* bytes);
+int kvb_gemm_sk_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
+                     void* workspace, size_t workspace_bytes, void* stream);
+/* Gate-up projection fused with SiluAndMul (linear.py:76-93 + activation.py:8-11)
+ * on the same schedule: w is the [2 * inter, K] merged weight with rows
+ * [gate | up]; each CTA multiplies 64 gate rows and the same features' 64 up
+ * rows; y[M, inter] = bf16(silu(bf16(x w_gate^T)) * bf16(x w_up^T)). */
+int kvb_gemm_sk_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M,
+                          int inter, int K, void* workspace, size_t workspace_bytes, void* stream);
+/* The stream-K GEMM's plan for this shape (host only; gated: N = inter):
+ * plan[0] token tile, plan[1] tiles, plan[2] K-steps per tile, plan[3] pairs
+ * (at most half the SMs; a launch may use fewer when fewer 2-CTA clusters fit). */
+int kvb_gemm_sk_plan(int M, int N, int K, int gated, int* plan);
+
 /* Process-wide tuning of kvb_gemm_bf16 / kvb_gemm_silu_bf16 (no reference
  * counterpart): the producer asks L2 for the weight K-steps `ksteps` ahead of
  * its TMA loads (cp.async.bulk.prefetch.tensor; 0 = off, the default; at most

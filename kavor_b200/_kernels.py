@@ -60,6 +60,33 @@ class _Workspace:
 WORKSPACE = _Workspace()
 
 
+class _ZeroedWorkspace(_Workspace):
+    """Per-device workspace of the stream-K GEMM: zero when allocated (its
+    hand-off flags must start at zero; every normal launch leaves them zero
+    again). One per device, used by launches that are ordered on one stream."""
+
+    def reserve(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        cur = self.buf.get(idx)
+        if cur is not None and cur.numel() >= nbytes:
+            return cur
+        _req(not torch.cuda.is_current_stream_capturing(),
+             f"GEMM workspace of {nbytes} bytes must be reserved before CUDA-graph capture")
+        if cur is not None:
+            self.retired.append(cur)
+        new = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        self.buf[idx] = new
+        return new
+
+    def reset(self) -> None:
+        """Zero every workspace again (after a device error bit: a hand-off wait gave up)."""
+        for t in self.buf.values():
+            t.zero_()
+
+
+GEMM_WORKSPACE = _ZeroedWorkspace()
+
+
 # ------------------------------------------------------------------ KV cache
 def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   slot_mapping: torch.Tensor) -> None:
@@ -80,7 +107,7 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
 
 # ------------------------------------------------------------------ norms
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """layernorm.py:319-342: 2-D [T, H] or 3-D strided [T, heads, H] input, new output tensor."""
+    """layernorm.py:235-258: 2-D [T, H] or 3-D strided [T, heads, H] input, new output tensor."""
     _cuda(x, "x", _BF16)
     _cuda(weight, "weight", _BF16)
     _req(x.stride(-1) == 1, "rmsnorm: last dim must be contiguous")
@@ -104,7 +131,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
 
 def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
                 out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """layernorm.py:344-372: residual updated in place, returns (out, residual)."""
+    """layernorm.py:260-288: residual updated in place, returns (out, residual)."""
     for t, n in ((x, "x"), (residual, "residual"), (weight, "weight")):
         _cuda(t, n, _BF16)
     _req(x.dim() == 2 and x.is_contiguous() and residual.is_contiguous() and x.shape == residual.shape,
@@ -338,6 +365,65 @@ def gemm_pair_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | No
         out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
     _lib.call("kvb_gemm_pair_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
               out.data_ptr(), out.stride(0), M, inter, K, splits, _stream())
+    return out
+
+
+def gemm_sk_plan(M: int, N: int, K: int, gated: bool = False) -> dict:
+    """Stream-K GEMM plan for this shape: token tile, tiles, K-steps per tile, pairs."""
+    out = (ctypes.c_int * 4)()
+    _lib.call("kvb_gemm_sk_plan", M, N, K, int(gated), out)
+    return {"mt": out[0], "tiles": out[1], "kb": out[2], "pairs": out[3]}
+
+
+def gemm_sk_workspace_bytes(M: int, N: int, K: int, gated: bool = False) -> int:
+    n = ctypes.c_size_t(0)
+    _lib.call("kvb_gemm_sk_workspace_size", M, N, K, int(gated), ctypes.byref(n))
+    return int(n.value)
+
+
+def _gemm_sk_args(x, weight, name, gated):
+    _cuda(x, "x", _BF16)
+    _cuda(weight, "weight", _BF16)
+    _req(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1], f"{name}: x [M, K], weight [N, K]")
+    _req(x.stride(1) == 1 and weight.stride(1) == 1, f"{name}: rows must be contiguous")
+    if gated:
+        _req(weight.shape[0] % 2 == 0, f"{name}: weight [2*I, K]")
+    M, K = x.shape
+    N = weight.shape[0] // 2 if gated else weight.shape[0]
+    ws = GEMM_WORKSPACE.reserve(max(gemm_sk_workspace_bytes(M, N, K, gated), _gemm_sk_workspace_max()), x.device)
+    return M, N, K, ws
+
+
+_SK_WS_MAX: int | None = None
+
+
+def _gemm_sk_workspace_max() -> int:
+    """The largest workspace any plan needs on this device (every pair, 256-token
+    tiles), reserved at the first call so that no later shape grows it (nor has
+    to during CUDA-graph capture)."""
+    global _SK_WS_MAX
+    if _SK_WS_MAX is None:
+        _SK_WS_MAX = gemm_sk_workspace_bytes(256, 1 << 20, 1 << 16)
+    return _SK_WS_MAX
+
+
+def gemm_sk(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ weight^T on CTA pairs with the stream-K schedule (bf16 in/out, fp32 accumulate)."""
+    M, N, K, ws = _gemm_sk_args(x, weight, "gemm_sk", False)
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    _lib.call("kvb_gemm_sk_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), out.data_ptr(),
+              out.stride(0), M, N, K, ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
+def gemm_sk_silu(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(x @ w_gate^T) * (x @ w_up^T) for the merged [gate | up] weight, stream-K CTA pairs."""
+    M, inter, K, ws = _gemm_sk_args(x, weight, "gemm_sk_silu", True)
+    if out is None:
+        out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
+    _lib.call("kvb_gemm_sk_silu_bf16", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0),
+              out.data_ptr(), out.stride(0), M, inter, K, ws.data_ptr(), ws.numel(), _stream())
     return out
 
 

@@ -45,6 +45,10 @@ SIGNATURES: dict[str, list] = {
     "kvb_gemm_pair_bf16": [P, L, P, L, P, L, I, I, I, I, P],
     "kvb_gemm_pair_silu_bf16": [P, L, P, L, P, L, I, I, I, I, P],
     "kvb_gemm_pair_plan": [I, I, I, I, I, POINTER(c_int)],
+    "kvb_gemm_sk_workspace_size": [I, I, I, I, POINTER(c_size_t)],
+    "kvb_gemm_sk_bf16": [P, L, P, L, P, L, I, I, I, P, c_size_t, P],
+    "kvb_gemm_sk_silu_bf16": [P, L, P, L, P, L, I, I, I, P, c_size_t, P],
+    "kvb_gemm_sk_plan": [I, I, I, I, POINTER(c_int)],
     "kvb_set_pdl": [I],
     "kvb_gemm_silu_workspace_size": [I, I, I, I, POINTER(c_size_t)],
     "kvb_gemm_silu_bf16": [P, L, P, L, P, L, I, I, I, I, P, c_size_t, P],
@@ -70,7 +74,7 @@ _QUERIES = {
     "kvb_gemm_workspace_size", "kvb_gemm_silu_workspace_size", "kvb_gemm_plan", "kvb_gemm_set_l2_prefetch",
     "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach",
     "kvb_comm_has_multicast", "kvb_comm_set_max_blocks", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
-    "kvb_comm_data_buffer", "kvb_comm_destroy",
+    "kvb_comm_data_buffer", "kvb_comm_destroy", "kvb_gemm_sk_workspace_size", "kvb_gemm_sk_plan",
 }
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.

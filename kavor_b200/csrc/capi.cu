@@ -38,6 +38,7 @@ int read_device_error_sampler(unsigned*, int);
 int read_device_error_gemm(unsigned*, int);
 int read_device_error_allreduce(unsigned*, int);
 int read_device_error_gemm_pair(unsigned*, int);
+int read_device_error_gemm_sk(unsigned*, int);
 int set_pdl_trigger_elementwise(int);
 int set_pdl_trigger_decode(int);
 int set_pdl_trigger_prefill(int);
@@ -45,6 +46,7 @@ int set_pdl_trigger_sampler(int);
 int set_pdl_trigger_gemm(int);
 int set_pdl_trigger_allreduce(int);
 int set_pdl_trigger_gemm_pair(int);
+int set_pdl_trigger_gemm_sk(int);
 
 }  // namespace kvb
 
@@ -60,7 +62,7 @@ extern "C" int kvb_device_error(unsigned* bits, int clear) {
   int (*readers[])(unsigned*, int) = {kvb::read_device_error_elementwise, kvb::read_device_error_decode,
                                       kvb::read_device_error_prefill, kvb::read_device_error_sampler,
                                       kvb::read_device_error_gemm, kvb::read_device_error_allreduce,
-                                      kvb::read_device_error_gemm_pair};
+                                      kvb::read_device_error_gemm_pair, kvb::read_device_error_gemm_sk};
   for (auto fn : readers) {
     int rc = fn(&w, clear);
     if (rc) return rc;
@@ -74,7 +76,8 @@ extern "C" int kvb_set_pdl(int enable) {
   if (enable != 0 && enable != 1) return kvb::set_error(kvb::kInvalid, "kvb_set_pdl: enable must be 0 or 1");
   int (*setters[])(int) = {kvb::set_pdl_trigger_elementwise, kvb::set_pdl_trigger_decode,
                            kvb::set_pdl_trigger_prefill, kvb::set_pdl_trigger_sampler, kvb::set_pdl_trigger_gemm,
-                           kvb::set_pdl_trigger_allreduce, kvb::set_pdl_trigger_gemm_pair};
+                           kvb::set_pdl_trigger_allreduce, kvb::set_pdl_trigger_gemm_pair,
+                           kvb::set_pdl_trigger_gemm_sk};
   for (auto fn : setters) {
     int rc = fn(enable);
     if (rc) return rc;

@@ -5,12 +5,14 @@ split the output rows across ranks (QKV rows ordered [q | k | v] per rank,
 gate/up rows [gate | up] per rank), row-parallel layers split the input
 columns and all-reduce the partial products (bias added on rank 0 only).
 All projections go through ``linear()``, the single GEMM entry point of the
-package. Which GEMM runs is a process-wide choice (``set_gemm_backend``):
-"cublas" (torch's F.linear, the reference's own GEMM; the default),
-"tcgen05" (this package's kernel, kvb_gemm_bf16, with the gate-up projection
-and SiluAndMul fused into kvb_gemm_silu_bf16 by the MLP) or "tcgen05_pair"
-(the CTA-pair kernel, kvb_gemm_pair_bf16, and its fused gate-up + SiLU form
-kvb_gemm_pair_silu_bf16).
+package, and the MLP's gate-up projection + SiluAndMul through
+``gate_up_silu()``. Which GEMM runs is a process-wide choice
+(``set_gemm_backend``): "cublas" (torch's F.linear, the reference's own GEMM;
+the default), "tcgen05" (this package's kernels: up to SK_MAX_TOKENS tokens
+the stream-K CTA-pair kernel kvb_gemm_sk_bf16 / kvb_gemm_sk_silu_bf16, above
+it the persistent single-CTA kernel kvb_gemm_bf16 / kvb_gemm_silu_bf16) or
+"tcgen05_pair" (the cluster-split CTA-pair kernel, kvb_gemm_pair_bf16, and
+its fused form kvb_gemm_pair_silu_bf16).
 """
 from __future__ import annotations
 
@@ -41,13 +43,22 @@ def gemm_backend() -> str:
     return _GEMM_BACKEND
 
 
+# Token counts at or below which the "tcgen05" backend runs the stream-K
+# CTA-pair kernel (decode batches); above, the persistent single-CTA kernel.
+SK_MAX_TOKENS = 256
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x W^T (+ b) in bf16 with fp32 accumulation."""
     if _GEMM_BACKEND != "cublas":
         from kavor_b200 import _kernels as K
 
-        y = (K.gemm if _GEMM_BACKEND == "tcgen05" else K.gemm_pair)(x, weight, out=out)
+        if _GEMM_BACKEND == "tcgen05":
+            fn = K.gemm_sk if x.shape[0] <= SK_MAX_TOKENS else K.gemm
+        else:
+            fn = K.gemm_pair
+        y = fn(x, weight, out=out)
         if bias is not None:
             y.add_(bias)
         return y
@@ -57,6 +68,20 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if bias is not None:
         out.add_(bias)
     return out
+
+
+def gate_up_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor | None:
+    """silu(x W_gate^T) * (x W_up^T) for the merged [gate | up] weight in one
+    kernel of the active backend (the reference's rounding points); None when
+    the backend has no fused form (cuBLAS: the caller runs the projection and
+    SiluAndMul)."""
+    if _GEMM_BACKEND == "cublas":
+        return None
+    from kavor_b200 import _kernels as K
+
+    if _GEMM_BACKEND == "tcgen05":
+        return (K.gemm_sk_silu if x.shape[0] <= SK_MAX_TOKENS else K.gemm_silu)(x, weight)
+    return K.gemm_pair_silu(x, weight)
 
 
 def _tp() -> tuple[int, int]:

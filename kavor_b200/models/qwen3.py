@@ -25,7 +25,7 @@ from kavor_b200.layers.attention import Attention
 from kavor_b200.layers.embed_head import ParallelLMHead, VocabParallelEmbedding
 from kavor_b200.layers.layernorm import RMSNorm
 from kavor_b200.layers.linear import (MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear, _tp,
-                                      gemm_backend)
+                                      gate_up_silu)
 from kavor_b200.layers.rotary_embedding import get_rope
 from kavor_b200.utils.context import context_scope, decode_rows, get_context
 
@@ -111,12 +111,10 @@ class Qwen3MLP(nn.Module):
         self.act_fn = SiluAndMul()
 
     def forward(self, x: torch.Tensor, reduce: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
-        backend = gemm_backend()
-        if backend == "tcgen05":  # gate-up projection and SiluAndMul in one kernel
-            return self.down_proj(K.gemm_silu(x, self.gate_up_proj.weight), reduce=reduce, out=out)
-        if backend == "tcgen05_pair":
-            return self.down_proj(K.gemm_pair_silu(x, self.gate_up_proj.weight), reduce=reduce, out=out)
-        return self.down_proj(self.act_fn(self.gate_up_proj(x)), reduce=reduce, out=out)
+        h = gate_up_silu(x, self.gate_up_proj.weight)  # gate-up projection and SiluAndMul in one kernel
+        if h is None:
+            h = self.act_fn(self.gate_up_proj(x))
+        return self.down_proj(h, reduce=reduce, out=out)
 
 
 class Qwen3DecoderLayer(nn.Module):

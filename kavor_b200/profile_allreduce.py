@@ -62,6 +62,39 @@ def _time_graph(fn, iters: int, warmup: int) -> float:
     return float(t.item())
 
 
+def fused_vs_nccl(ar: TPAllReduce, tokens: list[int], iters: int = 20, warmup: int = 3, seed: int = 1234) -> list[dict]:
+    """Per token count: the fused kernel in its automatic mode against NCCL
+    all_reduce followed by the add+RMSNorm kernel (the reference's sequence),
+    on the communicator ``ar`` (its hidden size, at most ar.max_tokens rows);
+    every rank calls it, rows are returned on every rank."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    H, dev = ar.hidden, ar.device
+    g = torch.Generator(device=dev).manual_seed(seed + rank)
+    tmax = max(tokens)
+    w = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16)
+    for i in range(2):
+        ar.buffers[i][:tmax].copy_(torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16))
+    nccl_x = [torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+    res = torch.randn(tmax, H, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(tmax, H, device=dev, dtype=torch.bfloat16)
+    rows = []
+    for T in tokens:
+        def fused(i, T=T):
+            _lib.call("kvb_allreduce_add_rmsnorm", ar.comm, i & 1, res.data_ptr(), res.data_ptr(), out.data_ptr(),
+                      w.data_ptr(), T, H, 1e-6, 0, torch.cuda.current_stream().cuda_stream)
+
+        def nccl(i, T=T):
+            x = nccl_x[i & 1][:T]
+            dist.all_reduce(x)
+            K.add_rmsnorm(x, res[:T], w, 1e-6, out=out[:T])
+
+        bus = 2 * (world - 1) / world * T * H * 2
+        tf, tn = _time_graph(fused, iters, warmup), _time_graph(nccl, iters, warmup)
+        rows.append({"hidden": H, "tokens": T, "fused_us": tf * 1e6, "nccl_plus_add_rmsnorm_us": tn * 1e6,
+                     "fused_busbw_gbs": bus / tf / 1e9, "nccl_busbw_gbs": bus / tn / 1e9})
+    return rows
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--hidden", default="1024,4096,5120")

@@ -8,7 +8,10 @@ cuBLAS (torch.matmul) on the same operands.
 variant runs at every L2 prefetch distance given (kvb_gemm_set_l2_prefetch);
 labels carry a "_pfN" suffix when N > 0. --pair adds the CTA-pair kernel
 (kvb_gemm_pair_bf16): "pair_auto" and "pair_sN" for K splits N <= 8, and
-"g_pair" (kvb_gemm_pair_silu_bf16) for the gate-up shapes.
+"g_pair" (kvb_gemm_pair_silu_bf16) for the gate-up shapes. The stream-K
+CTA-pair kernel (kvb_gemm_sk_bf16, "sk"; "g_sk" = kvb_gemm_sk_silu_bf16 for
+the gate-up shapes) is always measured; --no-single skips the single-CTA
+kernel's split sweep.
 
 Shapes: QKV, O, gate-up, down and LM head of Qwen3-8B at TP=1 and TP=8. Each
 timing is one replay of a CUDA graph of 20 launches (device time, CUDA events),
@@ -52,6 +55,7 @@ def main(argv=None) -> int:
     ap.add_argument("--splits", default="1,2,4,8,16")
     ap.add_argument("--l2-prefetch", default="0")
     ap.add_argument("--pair", action="store_true")
+    ap.add_argument("--no-single", action="store_true")
     a = ap.parse_args(argv)
     split_list = [int(v) for v in a.splits.split(",")]
     pf_list = [int(v) for v in a.l2_prefetch.split(",")]
@@ -74,7 +78,15 @@ def main(argv=None) -> int:
             ref = torch.matmul(x, ws[0].t())
             res = {"M": M, "shape": name, "N": N, "K": Kd, "copies": len(ws), "plan": K.gemm_plan(M, N, Kd)}
             nbytes = wbytes + M * Kd * 2 + M * N * 2
-            for pf in pf_list:
+            K.gemm_sk(x, ws[0], out=out)
+            err = (out.float() - ref.float()).abs().max().item()
+            t = _timeit(lambda i: K.gemm_sk(x, ws[i % len(ws)], out=out))
+            res["sk"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_sk_plan(M, N, Kd)["pairs"], round(err, 4)]
+            if name.startswith("gate_up"):
+                og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+                t = _timeit(lambda i: K.gemm_sk_silu(x, ws[i % len(ws)], out=og))
+                res["g_sk"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_sk_plan(M, N // 2, Kd, True)["pairs"]]
+            for pf in ([] if a.no_single else pf_list):
                 K.gemm_set_l2_prefetch(pf)
                 sfx = f"_pf{pf}" if pf else ""
                 for splits in [0] + split_list:

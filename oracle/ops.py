@@ -14,7 +14,7 @@ BF16 = torch.bfloat16
 
 # ------------------------------------------------------------------ norms
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """layernorm.py:8-39 (eager form :330-335): bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)."""
+    """layernorm.py:8-39 (eager form :246-251): bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)."""
     xf = x.float()
     rstd = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
     y = (xf * rstd).to(x.dtype)
@@ -22,7 +22,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float):
-    """layernorm.py:114-140 (eager form :367-372). Returns (out, new_residual);
+    """layernorm.py:114-140 (eager form :283-288). Returns (out, new_residual);
     the norm uses the fp32 sum, the residual is its bf16 rounding."""
     s = x.float() + residual.float()
     new_residual = s.to(x.dtype)

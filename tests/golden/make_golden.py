@@ -7,7 +7,7 @@ needed on the GPU box):
 
 What runs is the reference's own code on the CPU:
 * RMSNorm.rms_forward / add_rms_forward through their eager branches
-  (layernorm.py:330-335, :367-372; forced by lowering _MAX_FUSED_COLS);
+  (layernorm.py:246-251, :283-288; forced by lowering _MAX_FUSED_COLS);
 * RotaryEmbedding's cos_sin_cache (rotary_embedding.py:96-102) and the eager
   apply_rotary_emb / apply_rotary_emb_interleaved (:56-79);
 * SiluAndMul with torch.compile disabled (activation.py:8-11, eager); for the

@@ -96,8 +96,10 @@ def gemm_backend(request, monkeypatch):
     if request.param != "cublas":
         monkeypatch.setattr(K, "gemm", gemm)
         monkeypatch.setattr(K, "gemm_pair", gemm)
+        monkeypatch.setattr(K, "gemm_sk", gemm)
         monkeypatch.setattr(K, "gemm_silu", lambda x, w, out=None, splits=0: ops.silu_mul(ops.linear(x, w)))
         monkeypatch.setattr(K, "gemm_pair_silu", lambda x, w, out=None: ops.silu_mul(ops.linear(x, w)))
+        monkeypatch.setattr(K, "gemm_sk_silu", lambda x, w, out=None: ops.silu_mul(ops.linear(x, w)))
     L.set_gemm_backend(request.param)
     yield request.param
     L.set_gemm_backend("cublas")

@@ -57,7 +57,7 @@ def parse_args(argv=None):
     ap.add_argument("--context", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--gemm", choices=["cublas", "tcgen05", "tcgen05_pair"], default="cublas",
+    ap.add_argument("--gemm", choices=["auto", "cublas", "tcgen05", "tcgen05_pair"], default="auto",
                     help="GEMM of the projections (Config.gemm_backend)")
     ap.add_argument("--gemm-l2-prefetch", type=int, default=0,
                     help="tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads")
@@ -250,6 +250,29 @@ def run_reference(args) -> int:
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def gemm_dispatch(shape: dict, tp: int, batch: int, backend: str) -> dict:
+    """Which GEMM each projection of the decode step runs on (this rank's shapes)."""
+    from kavor_b200.layers.linear import SK_MAX_TOKENS, auto_uses_stream_k
+
+    H, I, hd = shape["hidden_size"], shape["intermediate_size"], 128
+    hq, hkv = shape["num_attention_heads"] // tp, shape["num_key_value_heads"] // tp
+    shapes = {"qkv": ((hq + 2 * hkv) * hd, H), "o": (H, hq * hd), "gate_up": (2 * I // tp, H),
+              "down": (H, I // tp), "lm_head": (shape["vocab_size"] // tp, H)}
+    ours = "kvb_gemm_sk_bf16 (stream-K CTA pairs)"
+    out = {}
+    for name, (N, K) in shapes.items():
+        if backend == "cublas" or (backend == "auto" and not auto_uses_stream_k(batch, N, K)):
+            out[name] = "cuBLAS (F.linear)" + (" + kvb_silu_mul" if name == "gate_up" else "")
+        elif backend == "tcgen05_pair":
+            out[name] = "kvb_gemm_pair" + ("_silu_bf16" if name == "gate_up" else "_bf16")
+        elif backend == "tcgen05" and batch > SK_MAX_TOKENS:
+            out[name] = "kvb_gemm" + ("_silu_bf16" if name == "gate_up" else "_bf16")
+        else:
+            out[name] = ("kvb_gemm_sk_silu_bf16 (stream-K CTA pairs, SiLU fused)" if name == "gate_up"
+                         and backend == "tcgen05" else ours)
+    return out
 
 
 def _config(args) -> dict:
@@ -498,10 +521,10 @@ def run_ours(args) -> int:
         e2e_pipelined = _e2e_pipelined_probe(runner, seqs, bm, args)
     # the decode step with the package's GEMM in place of cuBLAS (re-captured graphs; same guard)
     gemm_probes = None
-    if world == 1 and args.gemm == "cublas" and not args.no_probes:
+    if world == 1 and args.gemm == "auto" and not args.no_probes:
         graph = None  # the probes re-capture the decode graph
         gemm_probes = {f"{backend}_l2pf{pf}": _gemm_backend_probe(runner, seqs, B, args, backend, pf)
-                       for backend, pf in (("tcgen05", 0), ("tcgen05", 8))}
+                       for backend, pf in (("tcgen05", 0), ("cublas", 0))}
 
     if rank == 0:
         line = {
@@ -509,7 +532,8 @@ def run_ours(args) -> int:
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init weights (reference checkpoint shapes), random token ids, KV pages N(0,1)",
-            "config": _config(args), "decode_step_us": ms_per_step * 1e3, "attn_hbm_gbs": achieved,
+            "config": dict(_config(args), gemm_dispatch=gemm_dispatch(shape, world, B, args.gemm)),
+            "decode_step_us": ms_per_step * 1e3, "attn_hbm_gbs": achieved,
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches, "device_error_bits": dev_err,
         }
@@ -571,7 +595,7 @@ def _gemm_backend_probe(runner, seqs, B, args, backend: str, l2_prefetch: int) -
     except Exception as exc:  # the probe of an option that is off by default must not cost the main line
         return {"error": f"{type(exc).__name__}: {exc}"[:400]}
     finally:
-        set_gemm_backend("cublas")
+        set_gemm_backend(args.gemm)
         try:
             K.gemm_set_l2_prefetch(0)
         except Exception:

@@ -269,6 +269,11 @@ int kvb_gemm_sk_silu_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw
  * (at most half the SMs; a launch may use fewer when fewer 2-CTA clusters fit). */
 int kvb_gemm_sk_plan(int M, int N, int K, int gated, int* plan);
 
+/* Process-wide tuning of the stream-K GEMM (no reference counterpart): force
+ * the token tile (16..256, at most the batch's own; 0 = planned) and the pair
+ * count (0 = planned) of every later launch; used by tuning sweeps. */
+int kvb_gemm_sk_set_plan(int mt, int pairs);
+
 /* Process-wide tuning of kvb_gemm_bf16 / kvb_gemm_silu_bf16 (no reference
  * counterpart): the producer asks L2 for the weight K-steps `ksteps` ahead of
  * its TMA loads (cp.async.bulk.prefetch.tensor; 0 = off, the default; at most

@@ -375,6 +375,12 @@ def gemm_sk_plan(M: int, N: int, K: int, gated: bool = False) -> dict:
     return {"mt": out[0], "tiles": out[1], "kb": out[2], "pairs": out[3]}
 
 
+def gemm_sk_set_plan(mt: int = 0, pairs: int = 0) -> None:
+    """Force the stream-K GEMM's token tile and pair count for later launches
+    (0 = planned); a tuning knob for sweeps."""
+    _lib.call("kvb_gemm_sk_set_plan", int(mt), int(pairs))
+
+
 def gemm_sk_workspace_bytes(M: int, N: int, K: int, gated: bool = False) -> int:
     n = ctypes.c_size_t(0)
     _lib.call("kvb_gemm_sk_workspace_size", M, N, K, int(gated), ctypes.byref(n))

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, list] = {
     "kvb_gemm_sk_bf16": [P, L, P, L, P, L, I, I, I, P, c_size_t, P],
     "kvb_gemm_sk_silu_bf16": [P, L, P, L, P, L, I, I, I, P, c_size_t, P],
     "kvb_gemm_sk_plan": [I, I, I, I, POINTER(c_int)],
+    "kvb_gemm_sk_set_plan": [I, I],
     "kvb_set_pdl": [I],
     "kvb_gemm_silu_workspace_size": [I, I, I, I, POINTER(c_size_t)],
     "kvb_gemm_silu_bf16": [P, L, P, L, P, L, I, I, I, I, P, c_size_t, P],
@@ -75,6 +76,7 @@ _QUERIES = {
     "kvb_set_pdl", "kvb_gemm_pair_plan", "kvb_comm_ipc_handle_size", "kvb_comm_area_size", "kvb_comm_attach",
     "kvb_comm_has_multicast", "kvb_comm_set_max_blocks", "kvb_comm_result_rows", "kvb_allreduce_plan", "kvb_comm_create", "kvb_comm_open_peers",
     "kvb_comm_data_buffer", "kvb_comm_destroy", "kvb_gemm_sk_workspace_size", "kvb_gemm_sk_plan",
+    "kvb_gemm_sk_set_plan",
 }
 # Number of launching entry-point calls made so far (per name); used to count
 # the kernels a captured CUDA graph contains.

@@ -58,7 +58,7 @@ class Config:
     enable_prefix_caching: bool = True
     graph_batch_sizes: tuple[int, ...] | None = None  # decode buckets to capture (None: 1,2,4,8,16,32,...)
     fused_allreduce: bool = True  # TP > 1: NVLink all-reduce fused with add+RMSNorm (False: NCCL + separate norm)
-    gemm_backend: str = "cublas"  # projections: "cublas" (F.linear), "tcgen05" (kvb_gemm_bf16, fused gate-up+SiLU),
+    gemm_backend: str = "auto"  # projections: "auto" (stream-K kernel where it measured faster, F.linear elsewhere), "cublas" (F.linear), "tcgen05" (the package's kernels, fused gate-up+SiLU),
     #                               "tcgen05_pair" (kvb_gemm_pair_bf16)
     gemm_l2_prefetch: int = 0     # tcgen05 GEMM: weight K-steps prefetched into L2 ahead of the loads (0 = off)
     pdl: bool = False             # programmatic dependent launch of the package's kernels (kvb_set_pdl)
@@ -72,7 +72,7 @@ class Config:
         assert self.kvcache_block_size % 256 == 0, "kvcache_block_size must be a multiple of 256"
         assert 1 <= self.tensor_parallel_size <= 8
         assert self.load_format in ("auto", "dummy")
-        assert self.gemm_backend in ("cublas", "tcgen05", "tcgen05_pair"), "unknown gemm_backend"
+        assert self.gemm_backend in ("auto", "cublas", "tcgen05", "tcgen05_pair"), "unknown gemm_backend"
         assert 0 <= self.gemm_l2_prefetch <= 64
         assert self.decode_microbatches in (1, 2), "decode_microbatches must be 1 or 2"
         assert self.decode_microbatch_min_bs >= 2

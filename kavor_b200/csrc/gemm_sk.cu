@@ -10,8 +10,10 @@
 //
 // * pairs: two CTAs of a 2-CTA cluster issue one tcgen05.mma.cta_group::2 of
 //   M = 256 weight rows (128 in each CTA's shared memory) x N = MT tokens
-//   (MT/2 token rows staged in each CTA) x K = 16; a CTA moves 16 KB of weight
-//   and MT/2 x 128 B of tokens per 64-wide K step. Both CTAs' TMA loads (no
+//   (MT/2 token rows staged in each CTA) x K = 16. A stage is KC chunks of
+//   64 K: one 3-D TMA load of the CTA's 128 weight rows x KC chunks (KC x 16
+//   KB) and one of its MT/2 token rows (an SM streams one multi-chunk load at
+//   about twice the rate of separate 16 KB boxes). Both CTAs' loads (no
 //   multicast) complete on the even CTA's barrier; the MMA thread's commits
 //   release each stage in both CTAs;
 // * stream-K: the grid is one wave of persistent pairs (2-CTA clusters always
@@ -31,7 +33,8 @@
 //
 // Gated form: a pair tile is 128 output features; each CTA's 128 weight rows
 // are 64 gate rows [n, n + 64) and the matching 64 up rows [I + n, I + n + 64)
-// of the [gate | up] weight (two TMA boxes, weight layout unchanged), so gate
+// of the [gate | up] weight (a 4-D load whose third coordinate steps from the
+// gate to the up half; weight layout unchanged), so gate
 // and up of a feature sit in the same CTA's TMEM (lanes r and 64 + r); the up
 // warps hand bf16(up) to the gate warps through shared memory, which write
 // bf16(silu(bf16(gate)) * up) — the reference's rounding points.
@@ -55,7 +58,7 @@ KVB_DEFINE_ERROR_WORD(gemm_sk)
 namespace kvb {
 namespace {
 
-constexpr int kBK = 64;          // K elements per stage (one 128-byte swizzle row)
+constexpr int kBK = 64;          // K elements per chunk (one 128-byte swizzle row)
 constexpr int kRows = 128;       // weight rows per CTA (half of the pair's UMMA M)
 constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiWarp0 = 2;
@@ -80,25 +83,31 @@ struct SkArgs {
 template <int MT, bool G>
 struct SkCfg {
   static constexpr int kHalf = MT / 2;                    // token rows each CTA stages
-  static constexpr int kABytes = kRows * kBK * 2;         // 16 KB
-  static constexpr int kBBytes = kHalf * kBK * 2;
+  static constexpr int kKC = MT >= 128 ? 2 : 3;           // 64-wide K chunks per stage
+  static constexpr int kAChunk = kRows * kBK * 2;         // 16 KB of weight per chunk
+  static constexpr int kBChunk = kHalf * kBK * 2;
+  static constexpr int kABytes = kKC * kAChunk;
+  static constexpr int kBBytes = kKC * kBChunk;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kRing = 196 * 1024;
   static constexpr int kStagesRaw = kRing / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kChunk = MT < 32 ? MT : 32;        // tokens per TMEM load
   static constexpr int kTmemCols = 2 * MT < 32 ? 32 : 2 * MT;
   static constexpr int kXpose = 4 * 32 * kChunk * 2;      // per-warp bf16 transpose tiles
   static constexpr int kUp = G ? 2 * 64 * kChunk * 2 : 0; // gated: two chunks of up values, 64 features
   static constexpr int kSmem = kStages * kStageBytes + kXpose + kUp + 1024;
   static_assert(MT == 16 || MT == 32 || MT == 64 || MT == 128 || MT == 256, "token tile");
+  static_assert(kStages >= 3, "stage ring depth");
   static_assert(kSmem <= 227 * 1024, "dynamic shared memory of one CTA");
   static_assert(kTmemCols <= 512, "TMEM columns of one SM");
+  static_assert(kAChunk % 1024 == 0 && kBChunk % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 };
 
-// Pair p's iterations: [p * iters / pairs, (p + 1) * iters / pairs).
+// Pair p's iterations: [p * iters / pairs, (p + 1) * iters / pairs) (the host
+// keeps pairs * iters below 2^32, so the division is 32-bit).
 __device__ __forceinline__ long long range_lo(const SkArgs& a, int p) {
-  return (long long)p * a.iters / a.pairs;
+  return (long long)((uint32_t)p * (uint32_t)a.iters / (uint32_t)a.pairs);
 }
 
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
@@ -128,8 +137,8 @@ __device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
 
 // Bounded wait on an mbarrier phase that gives up at once when `dead` is set.
 __device__ __forceinline__ bool sk_wait(uint32_t bar, uint32_t parity, volatile int* dead) {
-  if (*dead) return false;
   if (mbar_try_wait(bar, parity)) return true;
+  if (*dead) return false;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*dead) return false;
@@ -211,38 +220,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tensormap(&wmap);
       prefetch_tensormap(&xmap);
+      // one thread, so the per-stage work is kept to a few dependent instructions:
+      // running slot / phase counters, shared-memory addresses advanced by a constant
       SegIter segs{lo, hi, a.kb};
       Seg sg;
-      uint32_t st = 0;
+      uint32_t issued = 0, phase = 0;
+      int s = 0;
+      const uint32_t ring0 = smem_u32(smem), full0 = smem_u32(&full_bar[0]), empty0 = smem_u32(&empty_bar[0]);
+      const uint32_t full0_leader = tc::map_to_rank(full0, leader);
       bool ok = true;
       while (ok && segs.next(sg)) {
         const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile - n_tile * a.m_tiles;
-        const int wrow = G ? n_tile * 128 + member * 64 : n_tile * 256 + member * kRows;
+        const int wrow = G ? n_tile * 128 + member * 64 : n_tile * 256 + member * kRows;  // gated: within a half
         const int xrow = m_tile * MT + member * C::kHalf;
-        for (int k = sg.k0; k < sg.k1; ++k, ++st) {
-          const int s = (int)(st % S);
-          if (st >= (uint32_t)S && !sk_wait(smem_u32(&empty_bar[s]), ((st / S) - 1) & 1, dead)) {
+        for (int k = sg.k0; k < sg.k1; ++k) {
+          if (issued >= (uint32_t)S && !sk_wait(empty0 + 8 * s, phase ^ 1u, dead)) {
             ok = false;
             break;
           }
-          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
-          const uint32_t fb = smem_u32(&full_bar[s]);
-          if (member == 0) mbar_arrive_expect_tx(fb, 2 * C::kStageBytes);
-          const uint32_t fl = tc::map_to_rank(fb, leader);
-          if (G) {  // 64 gate rows, then the same features' 64 up rows
-            tc::tma_load_2d_pair(sa, &wmap, k * kBK, wrow, fl);
-            tc::tma_load_2d_pair(sa + C::kABytes / 2, &wmap, k * kBK, a.up_row0 + wrow, fl);
-          } else {
-            tc::tma_load_2d_pair(sa, &wmap, k * kBK, wrow, fl);
+          const uint32_t sa = ring0 + (uint32_t)(s * C::kStageBytes);
+          const uint32_t fl = full0_leader + 8 * s;
+          if (member == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * C::kStageBytes);
+          // [chunk][128 weight rows][64 K] (gated: each chunk 64 gate rows, then the same features' up rows)
+          if (G) tc::tma_load_4d_pair(sa, &wmap, 0, wrow, 0, k * C::kKC, fl);
+          else tc::tma_load_3d_pair(sa, &wmap, 0, wrow, k * C::kKC, fl);
+          tc::tma_load_3d_pair(sa + C::kABytes, &xmap, 0, xrow, k * C::kKC, fl);
+          ++issued;
+          if (++s == S) {
+            s = 0;
+            phase ^= 1u;
           }
-          tc::tma_load_2d_pair(sa + C::kABytes, &xmap, k * kBK, xrow, fl);
         }
       }
       // before the CTA exits: the loads of the last stages have landed (leader's
       // barriers) and, after a normal run, the MMA thread's releases of them have
       // arrived on this CTA's barriers; one overall bound
       const long long t0 = clock64();
-      for (uint32_t i = st > (uint32_t)S ? st - S : 0; i < st; ++i) {
+      for (uint32_t i = issued > (uint32_t)S ? issued - S : 0; i < issued; ++i) {
         bool late = false;
         if (member == 0)
           while (!late && !mbar_try_wait(smem_u32(&full_bar[i % S]), (i / S) & 1)) late = clock64() - t0 > kSpinCycles;
@@ -256,26 +270,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && member == 0) {
       SegIter segs{lo, hi, a.kb};
       Seg sg;
-      uint32_t st = 0, j = 0;
+      uint32_t j = 0, phase = 0;
+      int s = 0;
+      const uint32_t full0 = smem_u32(&full_bar[0]), empty0 = smem_u32(&empty_bar[0]);
+      // descriptors of stage 0; a stage's are these plus its byte offset / 16 (the address field)
+      const uint64_t da0 = tc::smem_desc_sw128(smem_u32(smem)), db0 = tc::smem_desc_sw128(smem_u32(smem) + C::kABytes);
       bool ok = true;
       while (ok && segs.next(sg)) {
         const int b = (int)(j & 1);
         if (j >= 2 && !sk_wait(smem_u32(&tempty_bar[b]), ((j >> 1) - 1) & 1, dead)) break;
         tc::fence_after();
         const uint32_t d = tmem + (uint32_t)(b * MT);
-        for (int k = sg.k0; k < sg.k1; ++k, ++st) {
-          const int s = (int)(st % S);
-          if (!sk_wait(smem_u32(&full_bar[s]), (st / S) & 1, dead)) {
+        for (int k = sg.k0; k < sg.k1; ++k) {
+          if (!sk_wait(full0 + 8 * s, phase, dead)) {
             ok = false;
             break;
           }
           tc::fence_after();
-          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
-          const uint64_t da = tc::smem_desc_sw128(sa), db = tc::smem_desc_sw128(sa + C::kABytes);
+          const uint64_t off = (uint64_t)(s * (C::kStageBytes >> 4));
+          const uint64_t da = da0 + off, db = db0 + off;
+          tc::umma_pair_bf16(d, da, db, a.idesc, k > sg.k0 ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)  // +32 B along K inside the swizzle atom = +2 in the address field
-            tc::umma_pair_bf16(d, da + 2 * kk, db + 2 * kk, a.idesc, (k > sg.k0 || kk > 0) ? 1u : 0u);
-          tc::umma_commit_pair(smem_u32(&empty_bar[s]), pair_mask);
+          for (int kk = 1; kk < 4 * C::kKC; ++kk) {
+            // chunk kk / 4 sits a whole chunk further on; inside a chunk +32 B along K = +2
+            const uint64_t ca = (uint64_t)((kk >> 2) * (C::kAChunk >> 4) + 2 * (kk & 3));
+            const uint64_t cb = (uint64_t)((kk >> 2) * (C::kBChunk >> 4) + 2 * (kk & 3));
+            tc::umma_pair_bf16(d, da + ca, db + cb, a.idesc, 1u);
+          }
+          tc::umma_commit_pair(empty0 + 8 * s, pair_mask);
+          if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+          }
         }
         if (!ok) break;
         tc::umma_commit_pair(smem_u32(&tfull_bar[b]), pair_mask);
@@ -480,16 +506,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// [chunks of 64 K][rows][64 K] views: a 3-D map {64, rows, K / 64} whose box
+// is {64, box_rows, kc}, 128-byte swizzle; gated, a 4-D map {64, 64-row
+// blocks... } whose third coordinate steps from the gate half to the up half.
+int encode_chunks(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld, int box_rows, int kc,
+                  int64_t half_rows) {
   auto enc = tensor_map_encoder();
   if (!enc) return set_error(kNoEncoder, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (half_rows == 0) {
+    const cuuint64_t dims[3] = {(cuuint64_t)kBK, (cuuint64_t)rows, (cuuint64_t)(K / kBK)};
+    const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)kBK * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, (cuuint32_t)kc};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    // {64 K, rows of one half, 2 halves (gate, up), K / 64}; box {64, 64, 2, kc}
+    const cuuint64_t dims[4] = {(cuuint64_t)kBK, (cuuint64_t)half_rows, 2, (cuuint64_t)(K / kBK)};
+    const cuuint64_t strides[3] = {(cuuint64_t)ld * 2, (cuuint64_t)half_rows * ld * 2, (cuuint64_t)kBK * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 2, (cuuint32_t)kc};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return set_error(kEncode, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
   return kOk;
 }
@@ -514,38 +556,69 @@ int sk_stages(int mt) {
     default: return SkCfg<256, false>::kStages;
   }
 }
+int sk_kc(int mt) { return mt >= 128 ? SkCfg<256, false>::kKC : SkCfg<16, false>::kKC; }
 
 // Pairs: one wave (at most SMs / 2, and no more than fit together), and the
-// count with the smallest modelled time: the K steps of the longest range at
-// the per-SM weight rate — the HBM bandwidth shared by the streaming SMs, at
-// most what one SM's ring keeps in flight over the load latency — or at the
-// MMA rate, whichever is slower; plus, where tiles are cut, the owner reading
-// the other segments' partials. Ties go to more pairs.
-SkPlan make_sk_plan(int M, int N, int K, bool gated, int coresident = 0) {
+// count with the smallest modelled time. A pair's range of K steps runs at
+// the slowest of: the HBM bandwidth shared by the streaming SMs, one SM's
+// own load rate (about 110 GB/s for these multi-chunk loads) and the MMA rate
+// (64-wide K chunk x 4 MMAs of max(59, MT / 2) cycles). A tile cut into
+// pieces costs its owner the reading of the other pieces' fp32 partials and a
+// hand-off latency. Ties go to more pairs.
+SkPlan plan_for_tile(int M, int N, int K, bool gated, int mt, int max_pairs, double* cost) {
   SkPlan p;
-  p.mt = token_tile(M);
+  p.mt = mt;
   p.n_tiles = gated ? (N + 127) / 128 : (N + 255) / 256;
   p.m_tiles = (M + p.mt - 1) / p.mt;
-  p.kb = (K + kBK - 1) / kBK;
+  const int kc = sk_kc(p.mt);
+  p.kb = (K / kBK + kc - 1) / kc;
   p.iters = (long long)p.n_tiles * p.m_tiles * p.kb;
-  int max_pairs = std::min(kMaxPairs, device_sm_count() / 2);
-  if (coresident > 0) max_pairs = std::min(max_pairs, coresident);
-  const double hbm = 6.5e12, latency = 1.5e-6, mma_flops = 8192.0 * 1.8e9;
-  const double stage_w = 16384.0, stage_flop = 2.0 * kRows * p.mt * kBK;
-  const double sm_rate = sk_stages(p.mt) * stage_w / latency;
-  const double partial = (double)kRows * p.mt * 4, l2_rate = 100e9;
+  // every m-tile streams its n-tile's weights again (from HBM: the pieces of
+  // one n-tile's m-tiles do not run close enough together to meet in L2)
+  const double hbm = 6.8e12, sm_rate = 110e9, clk = 1.8e9;
+  const double stage_w = 16384.0 * kc;
+  const double t_mma = kc * 4 * std::max(59.0, p.mt / 2.0) / clk;
+  // a cut tile: the contributors write their fp32 partials while their SM
+  // streams the next segment, the owner reads them back (about 40 GB/s per
+  // SM end to end, measured), plus the flag hand-off
+  const double partial = (double)kRows * p.mt * 4, l2_rate = 40e9, handoff = 2e-6;
+  const double t_epi = (double)kRows * p.mt * 2 / 40e9;  // the last tile's drain (bf16 rows out)
   double best = -1;
   p.pairs = 1;
   for (int P = (int)std::min<long long>(max_pairs, p.iters); P >= 1; --P) {
     const long long per = (p.iters + P - 1) / P;
     const double rate = std::min(sm_rate, hbm / (2.0 * P));
-    const double t_stage = std::max(stage_w / rate, stage_flop / mma_flops);
+    const double t_stage = std::max(stage_w / rate, t_mma);
     const long long pieces = per >= p.kb ? (p.iters % P ? 2 : 1) : (p.kb + per - 1) / per + 1;
-    const double t = per * t_stage + (pieces - 1) * partial / l2_rate;
+    const double t = per * t_stage + t_epi + (pieces > 1 ? handoff + (pieces - 1) * partial / l2_rate : 0.0);
     if (best < 0 || t < best * 0.99) {
       best = t;
       p.pairs = P;
     }
+  }
+  *cost = best;
+  return p;
+}
+
+// Process-wide plan override for tuning sweeps (kvb_gemm_sk_set_plan):
+// token tile and pair count, 0 = the model's choice.
+std::atomic<int> g_sk_force_mt{0}, g_sk_force_pairs{0};
+
+SkPlan make_sk_plan(int M, int N, int K, bool gated, int coresident = 0) {
+  int max_pairs = std::min(kMaxPairs, device_sm_count() / 2);
+  if (coresident > 0) max_pairs = std::min(max_pairs, coresident);
+  double c1 = 0, c2 = 0;
+  const int mt = token_tile(M);
+  const int fmt = g_sk_force_mt.load(), fpairs = g_sk_force_pairs.load();
+  if (fmt > 0 || fpairs > 0) {
+    SkPlan p = plan_for_tile(M, N, K, gated, fmt > 0 && fmt <= mt ? fmt : mt, max_pairs, &c1);
+    if (fpairs > 0) p.pairs = (int)std::min<long long>(std::min(fpairs, max_pairs), p.iters);
+    return p;
+  }
+  SkPlan p = plan_for_tile(M, N, K, gated, mt, max_pairs, &c1);
+  if (mt == 256 && M <= 256) {  // two 128-token tiles: half the partials and the drain, a deeper ring
+    SkPlan q = plan_for_tile(M, N, K, gated, 128, max_pairs, &c2);
+    if (c2 < c1) p = q;
   }
   return p;
 }
@@ -640,21 +713,32 @@ int run_sk(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int6
     return set_error(kInvalid, "%s: bad sizes or leading dimensions", name);
   if (M == 0) return kOk;
   if (!x || !w || !y) return set_error(kInvalid, "%s: NULL pointer", name);
-  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ldx % 8 || ldw % 8 || K % 8)
-    return set_error(kInvalid, "%s: x/w rows must be 16-byte aligned (K, ldx, ldw multiples of 8)", name);
+  if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ldx % 8 || ldw % 8)
+    return set_error(kInvalid, "%s: x/w rows must be 16-byte aligned (ldx, ldw multiples of 8)", name);
+  if (K % kBK) return set_error(kUnsupported, "%s: K must be a multiple of 64 (got %d)", name, K);
+  if ((long long)((M + 15) / 16) * ((n_out + 127) / 128) * (K / kBK) * kMaxPairs >= (1ll << 32))
+    return set_error(kUnsupported, "%s: shape too large for the stream-K schedule", name);
+  // 2-CTA clusters of every variant fit the same way (one CTA per SM): the
+  // largest token tile's count bounds them all
   int coresident = 0;
   int rc = sk_coresident_for(token_tile(M), gated, &coresident);
   if (rc) return rc;
   const SkPlan p = make_sk_plan(M, n_out, K, gated, coresident);
+  if (p.mt != token_tile(M)) {  // the variant the plan chose gets its shared-memory limit too
+    int other = 0;
+    rc = sk_coresident_for(p.mt, gated, &other);
+    if (rc) return rc;
+  }
   const size_t need = sk_workspace_bytes(p);
   if (!workspace || ws_bytes < need)
     return set_error(kWorkspace, "%s: workspace of %zu bytes given, %zu needed (zeroed once when allocated)", name,
                      ws_bytes, need);
   if ((uintptr_t)workspace & 255) return set_error(kInvalid, "%s: workspace must be 256-byte aligned", name);
   CUtensorMap wmap, xmap;
-  rc = encode_rows(&wmap, w, (int64_t)n_out * (gated ? 2 : 1), K, ldw, gated ? 64 : kRows);
+  const int kc = sk_kc(p.mt);
+  rc = gated ? encode_chunks(&wmap, w, 0, K, ldw, 64, kc, n_out) : encode_chunks(&wmap, w, n_out, K, ldw, kRows, kc, 0);
   if (rc) return rc;
-  rc = encode_rows(&xmap, x, M, K, ldx, p.mt / 2);
+  rc = encode_chunks(&xmap, x, M, K, ldx, p.mt / 2, kc, 0);
   if (rc) return rc;
   SkArgs a;
   a.y = (bf16*)y;
@@ -701,9 +785,21 @@ extern "C" int kvb_gemm_sk_plan(int M, int N, int K, int gated, int* plan) {
   return kOk;
 }
 
+// An upper bound of what any launch of this shape needs on this device (a
+// launch may plan fewer pairs or a smaller token tile than a host-only query).
 extern "C" int kvb_gemm_sk_workspace_size(int M, int N, int K, int gated, size_t* bytes) {
   if (!bytes || M < 0 || N <= 0 || K <= 0) return set_error(kInvalid, "kvb_gemm_sk_workspace_size: bad sizes");
-  *bytes = M == 0 ? 0 : sk_workspace_bytes(make_sk_plan(M, N, K, gated != 0));
+  (void)gated;
+  const size_t pairs = (size_t)std::min(kMaxPairs, device_sm_count() / 2);
+  *bytes = M == 0 ? 0 : kFlagBytes + pairs * 2 * kRows * token_tile(M) * sizeof(float);
+  return kOk;
+}
+
+extern "C" int kvb_gemm_sk_set_plan(int mt, int pairs) {
+  if ((mt != 0 && mt != 16 && mt != 32 && mt != 64 && mt != 128 && mt != 256) || pairs < 0 || pairs > kMaxPairs)
+    return set_error(kInvalid, "kvb_gemm_sk_set_plan: token tile 0/16/32/64/128/256, pairs 0..%d", kMaxPairs);
+  g_sk_force_mt.store(mt);
+  g_sk_force_pairs.store(pairs);
   return kOk;
 }
 

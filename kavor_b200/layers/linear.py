@@ -7,8 +7,11 @@ columns and all-reduce the partial products (bias added on rank 0 only).
 All projections go through ``linear()``, the single GEMM entry point of the
 package, and the MLP's gate-up projection + SiluAndMul through
 ``gate_up_silu()``. Which GEMM runs is a process-wide choice
-(``set_gemm_backend``): "cublas" (torch's F.linear, the reference's own GEMM;
-the default), "tcgen05" (this package's kernels: up to SK_MAX_TOKENS tokens
+(``set_gemm_backend``): "auto" (the default: the package's stream-K kernel
+for decode batches on the weights where it measured faster than cuBLAS on the
+B200 — the full-vocabulary LM head — and torch's F.linear for the rest),
+"cublas" (torch's F.linear, the reference's own GEMM, everywhere), "tcgen05"
+(this package's kernels everywhere: up to SK_MAX_TOKENS tokens
 the stream-K CTA-pair kernel kvb_gemm_sk_bf16 / kvb_gemm_sk_silu_bf16, above
 it the persistent single-CTA kernel kvb_gemm_bf16 / kvb_gemm_silu_bf16) or
 "tcgen05_pair" (the cluster-split CTA-pair kernel, kvb_gemm_pair_bf16, and
@@ -28,8 +31,8 @@ def divide(numerator: int, denominator: int) -> int:
     return numerator // denominator
 
 
-GEMM_BACKENDS = ("cublas", "tcgen05", "tcgen05_pair")
-_GEMM_BACKEND = "cublas"
+GEMM_BACKENDS = ("auto", "cublas", "tcgen05", "tcgen05_pair")
+_GEMM_BACKEND = "auto"
 
 
 def set_gemm_backend(name: str) -> None:
@@ -46,16 +49,39 @@ def gemm_backend() -> str:
 # Token counts at or below which the "tcgen05" backend runs the stream-K
 # CTA-pair kernel (decode batches); above, the persistent single-CTA kernel.
 SK_MAX_TOKENS = 256
+# "auto": weights of at least this many elements run on the stream-K kernel at
+# decode batches. Measured on one B200 (graph-timed, weights streamed from HBM):
+# the Qwen3-8B LM head [151936, 4096] takes 183-257 us against cuBLAS's
+# 195-283 us from 1 to 256 tokens; every projection of a decoder layer and the
+# vocabulary shard at TP=8 ([18992, 4096]) is faster on cuBLAS.
+SK_AUTO_MIN_WEIGHT = 500_000_000
+
+
+def auto_uses_stream_k(M: int, N: int, K: int) -> bool:
+    """Whether the "auto" backend runs y[M, N] = x[M, K] W[N, K]^T on the
+    stream-K kernel (else F.linear)."""
+    return M <= SK_MAX_TOKENS and N * K >= SK_AUTO_MIN_WEIGHT and K % 64 == 0
+
+
+def _use_sk(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    return x.is_cuda and auto_uses_stream_k(x.shape[0], weight.shape[0], weight.shape[1])
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x W^T (+ b) in bf16 with fp32 accumulation."""
-    if _GEMM_BACKEND != "cublas":
+    if _GEMM_BACKEND == "auto" and _use_sk(x, weight):
+        from kavor_b200 import _kernels as K
+
+        y = K.gemm_sk(x, weight, out=out)
+        if bias is not None:
+            y.add_(bias)
+        return y
+    if _GEMM_BACKEND not in ("cublas", "auto"):
         from kavor_b200 import _kernels as K
 
         if _GEMM_BACKEND == "tcgen05":
-            fn = K.gemm_sk if x.shape[0] <= SK_MAX_TOKENS else K.gemm
+            fn = K.gemm_sk if x.shape[0] <= SK_MAX_TOKENS and x.shape[1] % 64 == 0 else K.gemm
         else:
             fn = K.gemm_pair
         y = fn(x, weight, out=out)
@@ -75,12 +101,12 @@ def gate_up_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor | None:
     kernel of the active backend (the reference's rounding points); None when
     the backend has no fused form (cuBLAS: the caller runs the projection and
     SiluAndMul)."""
-    if _GEMM_BACKEND == "cublas":
+    if _GEMM_BACKEND in ("cublas", "auto"):  # auto: no gate-up shape is faster fused (see SK_AUTO_MIN_WEIGHT)
         return None
     from kavor_b200 import _kernels as K
 
     if _GEMM_BACKEND == "tcgen05":
-        return (K.gemm_sk_silu if x.shape[0] <= SK_MAX_TOKENS else K.gemm_silu)(x, weight)
+        return (K.gemm_sk_silu if x.shape[0] <= SK_MAX_TOKENS and x.shape[1] % 64 == 0 else K.gemm_silu)(x, weight)
     return K.gemm_pair_silu(x, weight)
 
 

@@ -56,6 +56,8 @@ def main(argv=None) -> int:
     ap.add_argument("--l2-prefetch", default="0")
     ap.add_argument("--pair", action="store_true")
     ap.add_argument("--no-single", action="store_true")
+    ap.add_argument("--sk-plans", default="", help="also time the stream-K GEMM at forced (token tile x pairs), "
+                    "e.g. 128x32,256x64 (labels sk_<mt>x<pairs>)")
     a = ap.parse_args(argv)
     split_list = [int(v) for v in a.splits.split(",")]
     pf_list = [int(v) for v in a.l2_prefetch.split(",")]
@@ -86,6 +88,19 @@ def main(argv=None) -> int:
                 og = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
                 t = _timeit(lambda i: K.gemm_sk_silu(x, ws[i % len(ws)], out=og))
                 res["g_sk"] = [round(t, 2), round(nbytes / t / 1e3), K.gemm_sk_plan(M, N // 2, Kd, True)["pairs"]]
+            for spec in [v for v in a.sk_plans.split(",") if v]:
+                mt, pairs = (int(v) for v in spec.split("x"))
+                if mt > 16 and mt // 2 >= M:
+                    continue
+                K.gemm_sk_set_plan(mt, pairs)
+                try:
+                    t = _timeit(lambda i: K.gemm_sk(x, ws[i % len(ws)], out=out))
+                    res[f"sk_{mt}x{pairs}"] = round(t, 2)
+                    if name.startswith("gate_up"):
+                        t = _timeit(lambda i: K.gemm_sk_silu(x, ws[i % len(ws)], out=og))
+                        res[f"g_sk_{mt}x{pairs}"] = round(t, 2)
+                finally:
+                    K.gemm_sk_set_plan(0, 0)
             for pf in ([] if a.no_single else pf_list):
                 K.gemm_set_l2_prefetch(pf)
                 sfx = f"_pf{pf}" if pf else ""

@@ -89,6 +89,24 @@ def test_gemm_sk_is_deterministic_and_leaves_the_workspace_clean():
         torch.testing.assert_close(y.float(), x.float() @ w.float().t(), atol=1e-2, rtol=1e-2)
 
 
+def test_gemm_sk_first_call_in_a_fresh_process():
+    """A decode-batch shape whose plan uses a smaller token tile than the batch
+    (256 tokens as two 128-token tiles) as the process's first launch: every
+    kernel variant a plan picks is set up before it is launched."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = ("import torch; from kavor_b200 import _kernels as K; "
+            "x = torch.randn(256, 4096, device='cuda').to(torch.bfloat16); "
+            "w = (torch.randn(6144, 4096, device='cuda') * 0.02).to(torch.bfloat16); "
+            "y = K.gemm_sk(x, w); torch.cuda.synchronize(); "
+            "assert (y.float() - x.float() @ w.float().t()).abs().max().item() < 5e-2")
+    root = str(Path(__file__).resolve().parents[1])
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
 def test_gemm_sk_graph_replay():
     """Three projections captured in one CUDA graph, replayed with new inputs."""
     from kavor_b200 import _kernels as K_

@@ -45,7 +45,7 @@ def gemm_backend(request):
     try:
         yield request.param
     finally:
-        set_gemm_backend("cublas")
+        set_gemm_backend("auto")
 
 
 BACKENDS = ["cublas", "tcgen05", "tcgen05_pair"]

@@ -82,7 +82,7 @@ def _model(cfg):
 CASES = [("qwen3", "tiny_model_golden.pt")] + [(f, f"{f}_tiny_golden.pt") for f in cases.FAMILIES]
 
 
-@pytest.fixture(params=["cublas", "tcgen05", "tcgen05_pair"])
+@pytest.fixture(params=["auto", "cublas", "tcgen05", "tcgen05_pair"])
 def gemm_backend(request, monkeypatch):
     """Every GEMM backend of linear(): torch's F.linear, or the package's
     kernel entry points (replaced here by the oracle's linear, with the gate-up
@@ -102,7 +102,7 @@ def gemm_backend(request, monkeypatch):
         monkeypatch.setattr(K, "gemm_sk_silu", lambda x, w, out=None: ops.silu_mul(ops.linear(x, w)))
     L.set_gemm_backend(request.param)
     yield request.param
-    L.set_gemm_backend("cublas")
+    L.set_gemm_backend("auto")
 
 
 @pytest.mark.parametrize("family,fixture", CASES, ids=[c[0] for c in CASES])
@@ -144,7 +144,19 @@ def test_gemm_backend_names():
 
     with pytest.raises(ValueError, match="unknown GEMM backend"):
         L.set_gemm_backend("triton")
-    assert L.gemm_backend() == "cublas"
+    assert L.gemm_backend() == "auto"
+
+
+def test_auto_gemm_dispatch_rule():
+    """The default backend puts the full-vocabulary LM head of Qwen3-8B on the
+    stream-K kernel at decode batches and every decoder-layer projection (and
+    the TP=8 vocabulary shard, and prefill batches) on F.linear."""
+    from kavor_b200.layers import linear as L
+
+    assert L.auto_uses_stream_k(256, 151936, 4096) and L.auto_uses_stream_k(1, 151936, 4096)
+    assert not L.auto_uses_stream_k(257, 151936, 4096)
+    for N, K in ((6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288), (18992, 4096), (151936, 1024)):
+        assert not L.auto_uses_stream_k(256, N, K), (N, K)
 
 
 def test_family_attention_flags():

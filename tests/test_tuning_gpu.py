@@ -187,7 +187,7 @@ def test_tcgen05_gemm_backend_replays_reference_greedy(prefetch):
         gold = torch.load(GOLDEN / "tiny_model_golden.pt", weights_only=False)
         checked = sum(cases.check_greedy_step(logits, rec) for logits, rec in cases.replay(gold, step))
     finally:
-        set_gemm_backend("cublas")
+        set_gemm_backend("auto")
         K_.gemm_set_l2_prefetch(0)
     assert checked >= 13
 
@@ -210,7 +210,7 @@ def test_programmatic_dependent_launch_changes_no_result(tiny_dir, gemm):
         finally:
             runner.exit()
             K_.set_pdl(False)
-            set_gemm_backend("cublas")
+            set_gemm_backend("auto")
     assert runs[0] == runs[1]
 
 

@@ -323,7 +323,7 @@ def run_ours(args) -> int:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     else:
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_free_port()}", world_size=1, rank=0,
                                 device_id=dev)

@@ -56,6 +56,10 @@ def main(argv=None) -> int:
     ap.add_argument("--l2-prefetch", default="0")
     ap.add_argument("--pair", action="store_true")
     ap.add_argument("--no-single", action="store_true")
+    ap.add_argument("--launches", type=int, default=0,
+                    help="profiler mode: only N plain launches of --impl on --shape at the first M (no timing)")
+    ap.add_argument("--shape", default="lm_head_tp1")
+    ap.add_argument("--impl", default="sk", choices=["sk", "sk_silu", "single", "cublas"])
     ap.add_argument("--sk-plans", default="", help="also time the stream-K GEMM at forced (token tile x pairs), "
                     "e.g. 128x32,256x64 (labels sk_<mt>x<pairs>)")
     a = ap.parse_args(argv)
@@ -70,6 +74,8 @@ def main(argv=None) -> int:
                             ("down", 4096, 12288 // tp), ("lm_head", 151936 // tp, 4096)):
             shapes.append((f"{name}_tp{tp}", N, Kd))
     Ms = [int(x) for x in a.ms.split(",")]
+    if a.launches:
+        return _plain_launches(dict((n, (N, Kd)) for n, N, Kd in shapes)[a.shape], Ms[0], a.impl, a.launches, dev)
     for M in Ms:
         for name, N, Kd in shapes:
             wbytes = N * Kd * 2
@@ -156,6 +162,28 @@ def main(argv=None) -> int:
                 res[k + "_tflops"] = 2 * M * N * Kd / res[k + "_us"] / 1e6
             print(json.dumps(res), flush=True)
     return 0
+
+
+def _plain_launches(shape, M: int, impl: str, n: int, dev) -> int:
+    """n back-to-back launches of one GEMM on fresh weights (for ncu: one
+    shape, a few launches, a few GB on the device at most)."""
+    N, Kd = shape
+    x = torch.randn(M, Kd, device=dev).to(torch.bfloat16)
+    ws = [(torch.randn(N, Kd, device=dev) * 0.02).to(torch.bfloat16) for _ in range(2)]
+    for i in range(n):
+        w = ws[i % 2]
+        if impl == "sk":
+            K.gemm_sk(x, w)
+        elif impl == "sk_silu":
+            K.gemm_sk_silu(x, w)
+        elif impl == "single":
+            K.gemm(x, w)
+        else:
+            torch.matmul(x, w.t())
+    torch.cuda.synchronize()
+    bits = _lib.device_error(clear=True)
+    print(json.dumps({"M": M, "N": N, "K": Kd, "impl": impl, "launches": n, "device_error_bits": bits}))
+    return 1 if bits else 0
 
 
 if __name__ == "__main__":

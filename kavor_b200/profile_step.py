@@ -40,7 +40,7 @@ def main(argv=None) -> int:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     else:
         import socket
 

@@ -395,6 +395,7 @@ def run_ours(args) -> int:
     # --- the decode-scaling batch sizes below B: the first b
     # sequences, every one at context ctx0, each size's captured graph replayed
     batch_sweep = {}
+    gb = None
     for b in sweep:
         runner.run(seqs[:b], False)  # static inputs of bucket b
         gb = runner.graphs[next(x for x in runner.graph_bs if x >= b)]
@@ -414,6 +415,10 @@ def run_ours(args) -> int:
                      allreduce_bus_bytes(shape, world, b) / (NVLINK_GBS * 1e9))
         batch_sweep[str(b)] = {"tok_s": b * args.steps / tb, "ms_per_step": tb / args.steps * 1e3,
                                "step_roofline_frac": roof_b / (tb / args.steps)}
+    # at TP > 1 a decode graph holds NCCL work (the vocab-shard sampling
+    # all-gather): no reference may outlive the runner, or destroying the
+    # process group waits for good
+    gb = None
     runner.run(seqs, False)  # back to the full batch
 
     # --- decode attention alone, rotating over the layers' caches (no L2 reuse)
@@ -547,7 +552,7 @@ def run_ours(args) -> int:
             line["gemm_backend_probes"] = gemm_probes
         print(json.dumps(line), flush=True)
     # graphs hold NCCL work: every reference must be gone before the group is destroyed
-    del graph
+    del graph, gb
     try:
         runner.exit()
         torch.cuda.synchronize()

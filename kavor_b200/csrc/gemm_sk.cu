@@ -211,11 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_before();
   tc::cluster_sync_all();  // both CTAs' barriers and the pair's TMEM exist before either signals the other's
   tc::fence_after();
-  // token rows, outputs and the workspace belong to the kernels before this one:
-  // every thread waits for them here, except the producer, which first asks
-  // for its first stages' weights (no kernel writes them; under programmatic
-  // dependent launch those loads overlap the previous kernel's end)
-  if (threadIdx.x != 0) kernel_entry();
+  kernel_entry();          // token rows, outputs and the workspace belong to the kernels before this one
   const uint32_t tmem = tmem_base_s;
   const long long lo = range_lo(a, pair), hi = range_lo(a, pair + 1);
 
@@ -232,23 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       const uint32_t ring0 = smem_u32(smem), full0 = smem_u32(&full_bar[0]), empty0 = smem_u32(&empty_bar[0]);
       const uint32_t full0_leader = tc::map_to_rank(full0, leader);
-      // weights of the first (up to S) stages before the grid dependency
-      uint32_t pre = 0;
-      {
-        SegIter pseg{lo, hi, a.kb};
-        Seg ps;
-        while (pre < (uint32_t)S && pseg.next(ps)) {
-          const int n_tile = ps.tile / a.m_tiles;
-          const int wrow = G ? n_tile * 128 + member * 64 : n_tile * 256 + member * kRows;
-          for (int k = ps.k0; k < ps.k1 && pre < (uint32_t)S; ++k, ++pre) {
-            const uint32_t sa = ring0 + pre * (uint32_t)C::kStageBytes;
-            if (member == 0) mbar_arrive_expect_tx(full0 + 8 * pre, 2 * C::kStageBytes);
-            if (G) tc::tma_load_4d_pair(sa, &wmap, 0, wrow, 0, k * C::kKC, full0_leader + 8 * pre);
-            else tc::tma_load_3d_pair(sa, &wmap, 0, wrow, k * C::kKC, full0_leader + 8 * pre);
-          }
-        }
-      }
-      kernel_entry();
       bool ok = true;
       while (ok && segs.next(sg)) {
         const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile - n_tile * a.m_tiles;
@@ -261,12 +240,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t sa = ring0 + (uint32_t)(s * C::kStageBytes);
           const uint32_t fl = full0_leader + 8 * s;
-          if (issued >= pre) {  // (the first stages' weights are on their way already)
-            if (member == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * C::kStageBytes);
-            // [chunk][128 weight rows][64 K] (gated: each chunk 64 gate rows, then the same features' up rows)
-            if (G) tc::tma_load_4d_pair(sa, &wmap, 0, wrow, 0, k * C::kKC, fl);
-            else tc::tma_load_3d_pair(sa, &wmap, 0, wrow, k * C::kKC, fl);
-          }
+          if (member == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * C::kStageBytes);
+          // [chunk][128 weight rows][64 K] (gated: each chunk 64 gate rows, then the same features' up rows)
+          if (G) tc::tma_load_4d_pair(sa, &wmap, 0, wrow, 0, k * C::kKC, fl);
+          else tc::tma_load_3d_pair(sa, &wmap, 0, wrow, k * C::kKC, fl);
           tc::tma_load_3d_pair(sa + C::kABytes, &xmap, 0, xrow, k * C::kKC, fl);
           ++issued;
           if (++s == S) {

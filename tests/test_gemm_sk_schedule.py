@@ -100,10 +100,10 @@ def test_every_pair_count_hands_off_every_partial_once(tiles, kb):
 
 def test_the_model_finds_a_broken_rule():
     """The checks are not vacuous: dealing the same ranges to the pairs in
-    reverse order (pair 0 the last range, ...) makes every cut tile's owner
-    the FIRST segment of its pair and its contributors last segments — a pair
-    would then wait, at its start, on pieces other pairs only reach at their
-    end — and the model rejects it; so does an empty range."""
+    reverse order (pair 0 the last range, ...) breaks the owner's rule for
+    finding its contributors (the pairs after it whose range starts inside
+    its tile): the listed pairs are no longer the tile's later pieces, and the
+    model rejects it; so does an empty range."""
     tiles, kb, pairs = 24, 32, 70
     iters = tiles * kb
     fwd = [(range_lo(p, iters, pairs), range_lo(p + 1, iters, pairs)) for p in range(pairs)]

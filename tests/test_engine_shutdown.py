@@ -45,7 +45,9 @@ def _idle_worker(marker):
     from kavor_b200.engine.model_runner import ModelRunner
 
     # should the product code never notice its parent is gone, the test still leaves no process behind
-    threading.Timer(120.0, lambda: os._exit(3)).start()
+    guard = threading.Timer(120.0, lambda: os._exit(3))
+    guard.daemon = True
+    guard.start()
 
     ev = mp.get_context("spawn").Event()  # never set: rank 0 sends nothing
     runner = SimpleNamespace(event=ev, rank=1, shm=None)

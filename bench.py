@@ -557,7 +557,12 @@ def run_ours(args) -> int:
         runner.exit()
         torch.cuda.synchronize()
         barrier()
+        # past the last barrier nothing runs on any GPU; should destroying the group
+        # still wait (a graph holding NCCL work outlived it), the line is printed:
+        # say so and leave instead of holding every rank until the launcher's limit
+        guard = _exit_if_stuck(TEARDOWN_LIMIT_S)
         dist.destroy_process_group()
+        guard.cancel()
     except Exception:
         probes = [e2e_pipelined] + list((gemm_probes or {}).values())
         if not any(p is not None and "error" in p for p in probes):
@@ -627,6 +632,21 @@ def _e2e_pipelined_probe(runner, seqs, bm, args) -> dict:
                 "device_error_bits": _lib.device_error(clear=True)}
     except Exception as exc:  # the probe of an option that is off by default must not cost the main line
         return {"error": f"{type(exc).__name__}: {exc}"[:400]}
+
+
+TEARDOWN_LIMIT_S = 90.0
+
+
+def _exit_if_stuck(seconds: float) -> threading.Timer:
+    def fire():
+        print(f"bench.py: the process group was not destroyed within {seconds:.0f} s of the final barrier "
+              "(the result line is printed above); exiting", file=sys.stderr, flush=True)
+        os._exit(0)
+
+    t = threading.Timer(seconds, fire)
+    t.daemon = True
+    t.start()
+    return t
 
 
 def _free_port() -> int:

@@ -72,3 +72,14 @@ def test_reference_arm_line(monkeypatch, capsys):
     assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert "ramp fills" in line["cpu_baseline"]["sample"]
+
+
+def test_teardown_guard_is_cancelled_in_time():
+    """The guard around destroying the process group fires only after its
+    limit; cancelled before that, it does nothing."""
+    import time
+
+    t = bench._exit_if_stuck(5.0)
+    time.sleep(0.05)
+    t.cancel()
+    assert not t.is_alive() or t.finished.is_set()

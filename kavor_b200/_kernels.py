@@ -78,13 +78,20 @@ class _ZeroedWorkspace(_Workspace):
         self.buf[idx] = new
         return new
 
-    def reset(self) -> None:
-        """Zero every workspace again (after a device error bit: a hand-off wait gave up)."""
-        for t in self.buf.values():
-            t.zero_()
+    def reset(self, bits: int = 0) -> None:
+        """Zero every workspace again. A hand-off wait that gave up leaves the
+        flags it did not consume raised, which a later launch would take for
+        fresh partials; so this runs whenever the device error bits are read
+        and cleared (the read synchronised the device, and the zeroing is
+        finished before the next launch on any stream)."""
+        for idx, t in self.buf.items():
+            with torch.cuda.device(idx):
+                t.zero_()
+                torch.cuda.synchronize()
 
 
 GEMM_WORKSPACE = _ZeroedWorkspace()
+_lib.on_cleared_device_error(GEMM_WORKSPACE.reset)
 
 
 # ------------------------------------------------------------------ KV cache

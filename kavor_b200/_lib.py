@@ -127,8 +127,23 @@ def launch_count() -> int:
     return sum(CALLS.values())
 
 
+# Called with the bits when device_error(clear=True) reads and clears a
+# non-zero word: state that a kernel which gave up may have left behind (the
+# stream-K GEMM's hand-off flags) is reset there, so no later launch reads it.
+_ON_CLEARED_ERROR: list = []
+
+
+def on_cleared_device_error(fn) -> None:
+    """Register ``fn(bits)``, run after device_error(clear=True) cleared non-zero bits."""
+    if fn not in _ON_CLEARED_ERROR:
+        _ON_CLEARED_ERROR.append(fn)
+
+
 def device_error(clear: bool = True) -> int:
     """Device-side error bits of the current device (synchronises)."""
     bits = c_uint(0)
     call("kvb_device_error", ctypes.byref(bits), 1 if clear else 0)
+    if clear and bits.value:
+        for fn in _ON_CLEARED_ERROR:
+            fn(int(bits.value))
     return int(bits.value)

@@ -170,3 +170,25 @@ def test_allreduce_plan_matches_the_documented_choice(lib):
     assert allreduce_plan(2, False, 5, H, mode=2) == {"peer_two_shot": 1, "switch": 0}
     assert allreduce_plan(8, True, 5, H, mode=4)["switch"] == 2
     assert allreduce_plan(8, True, 4096, H, mode=1) == {"peer_two_shot": 0, "switch": 0}
+
+
+def test_clearing_device_error_bits_runs_the_reset_hooks(monkeypatch):
+    """A kernel that gave up a wait may leave state behind (the stream-K GEMM's
+    raised hand-off flags); reading and clearing non-zero error bits runs the
+    registered resets, and the stream-K workspace's reset is one of them."""
+    from kavor_b200 import _kernels, _lib
+
+    assert _kernels.GEMM_WORKSPACE.reset in _lib._ON_CLEARED_ERROR
+    seen = []
+    monkeypatch.setattr(_lib, "_ON_CLEARED_ERROR", [seen.append])
+    word = {"bits": 0}
+
+    def fake_call(name, *args):
+        assert name == "kvb_device_error"
+        args[0]._obj.value = word["bits"]
+
+    monkeypatch.setattr(_lib, "call", fake_call)
+    assert _lib.device_error(clear=True) == 0 and seen == []
+    word["bits"] = 4
+    assert _lib.device_error(clear=False) == 4 and seen == []  # read only: nothing is reset
+    assert _lib.device_error(clear=True) == 4 and seen == [4]

@@ -140,6 +140,14 @@ class BlockManager:
         if len(seq) % self.block_size == 1:
             seq.block_table.append(self.allocate_block())
 
+    def may_append_blocks(self, seqs: list[Sequence]) -> None:
+        """may_append_block for every sequence of a decode batch, in order (one
+        Python frame for the batch: this runs on the host every decode step)."""
+        bs = self.block_size
+        for seq in seqs:
+            if seq.num_tokens % bs == 1:
+                seq.block_table.append(self.allocate_block())
+
     def hash_blocks(self, seq: Sequence) -> None:
         """Key every block completed by this step so later prompts can reuse it."""
         if not self.enable_prefix_cache:

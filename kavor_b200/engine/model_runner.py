@@ -19,6 +19,7 @@ from __future__ import annotations
 import datetime
 import itertools
 import multiprocessing
+import operator
 import os
 import pickle
 import time
@@ -44,6 +45,12 @@ MAILBOX_POLL_S = 1.0   # a worker checks that rank 0's process is still alive th
 
 
 # ----------------------------------------------------------------- host metadata
+_NUM_TOKENS = operator.attrgetter("num_tokens")
+_LAST_TOKEN = operator.attrgetter("last_token")
+_BLOCK_TABLE = operator.attrgetter("block_table")
+_TEMPERATURE = operator.attrgetter("temperature")
+
+
 def block_table_matrix(seqs: list[Sequence], width: int | None = None) -> np.ndarray:
     """[B, max blocks] int32, rows padded with -1 (model_runner.py:469-473).
     One flat gather of every table and one masked scatter (no per-row numpy
@@ -59,18 +66,28 @@ def block_table_matrix(seqs: list[Sequence], width: int | None = None) -> np.nda
 def decode_metadata(seqs: list[Sequence], block_size: int) -> dict[str, np.ndarray]:
     """model_runner.py:448-467: the last token of every sequence at position len-1,
     written to slot block_table[-1]*block_size + last_block_num_tokens - 1.
-    One pass over the sequences (token, length, last block id, tokens in it)."""
+    Attributes are pulled with C-level getters (no Python frame per sequence)
+    and the last block id comes from the block-table matrix."""
     n = len(seqs)
-    rows = np.fromiter(itertools.chain.from_iterable(
-        (s.last_token, s.num_tokens, s.block_table[-1]) for s in seqs), np.int64, 3 * n).reshape(n, 3)
-    ctx = rows[:, 1]
+    ctx = np.fromiter(map(_NUM_TOKENS, seqs), np.int64, n)
+    tables = list(map(_BLOCK_TABLE, seqs))
+    lens = np.fromiter(map(len, tables), np.int64, n)
+    if n and int(lens.min()) == 0:
+        raise ValueError("decode_metadata: every decoding sequence needs a block")
+    w = int(lens.max(initial=0))
+    bt = np.full((n, w), -1, dtype=np.int32)
+    if w:
+        bt[np.arange(w) < lens[:, None]] = np.fromiter(itertools.chain.from_iterable(tables), np.int32,
+                                                       int(lens.sum()))
+    pos = ctx - 1
+    last_block = bt[np.arange(n), lens - 1].astype(np.int64)
     return {
-        "input_ids": rows[:, 0].copy(),
-        "positions": ctx - 1,
+        "input_ids": np.fromiter(map(_LAST_TOKEN, seqs), np.int64, n),
+        "positions": pos,
         # last_block_num_tokens - 1 == (len - 1) % block_size
-        "slot_mapping": (rows[:, 2] * block_size + (ctx - 1) % block_size).astype(np.int32),
+        "slot_mapping": (last_block * block_size + pos % block_size).astype(np.int32),
         "context_lens": ctx.astype(np.int32),
-        "block_tables": block_table_matrix(seqs),
+        "block_tables": bt,
     }
 
 
@@ -225,16 +242,14 @@ def advance_decode(runner, seqs: list[Sequence], block_manager, steps: int, pipe
     way while the host's per-step work overlaps the GPU's."""
     if not pipelined:
         for _ in range(steps):
-            for s in seqs:
-                block_manager.may_append_block(s)
+            block_manager.may_append_blocks(seqs)
             for s, t in zip(seqs, runner.run(seqs, False)):
                 s.num_cached_tokens += 1
                 s.append_token(t)
         return
     pending = None
     for _ in range(steps):
-        for s in seqs:
-            block_manager.may_append_block(s)
+        block_manager.may_append_blocks(seqs)
         nxt = runner.run_async(seqs, chain=pending is not None)
         if pending is not None:
             for s, t in zip(seqs, pending.result()):
@@ -578,7 +593,7 @@ class ModelRunner:
     def _step_metadata(self, seqs: list[Sequence], is_prefill: bool) -> tuple[dict, np.ndarray]:
         """The host arrays of one model step: prefill_metadata / decode_metadata
         and the sampling temperatures."""
-        temps = np.fromiter((s.temperature for s in seqs), np.float32, len(seqs))
+        temps = np.fromiter(map(_TEMPERATURE, seqs), np.float32, len(seqs))
         if is_prefill:
             return prefill_metadata(seqs, self.block_size), temps
         return decode_metadata(seqs, self.block_size), temps

@@ -74,3 +74,24 @@ def test_pool_stays_consistent(make_seq, program):
         bm.deallocate(s)
     _check(bm, [])
     assert len(bm.free_block_ids) == POOL
+
+
+@settings(max_examples=50, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(st.lists(st.integers(1, 3 * BS), min_size=1, max_size=5), st.integers(1, 2 * BS))
+def test_batched_may_append_equals_the_per_sequence_call(make_seq, lengths, steps):
+    """may_append_blocks(batch) takes the same blocks, in the same order, as
+    may_append_block over the batch, step after step."""
+    pools = [BlockManager(POOL * 8, BS, enable_prefix_cache=False) for _ in range(2)]
+    batches = [[make_seq(range(n)) for n in lengths] for _ in range(2)]
+    for bm, seqs in zip(pools, batches):
+        for s in seqs:
+            bm.allocate_prefill(s, 0)
+    for _ in range(steps):
+        for s in batches[0]:
+            pools[0].may_append_block(s)
+        pools[1].may_append_blocks(batches[1])
+        assert [s.block_table for s in batches[0]] == [s.block_table for s in batches[1]]
+        for seqs in batches:
+            for s in seqs:
+                s.append_token(0)
+    assert pools[0].free_block_ids == pools[1].free_block_ids

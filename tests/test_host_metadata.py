@@ -99,6 +99,20 @@ def test_vectorised_metadata_equals_reference_loops_on_random_states():
         a, b = decode_metadata(dseqs, bs), ohost.prepare_decode(dseqs, bs)
         for k in b:
             assert a[k].tolist() == b[k], k
+        dtypes = {"input_ids": np.int64, "positions": np.int64, "slot_mapping": np.int32, "context_lens": np.int32,
+                  "block_tables": np.int32}
+        assert {k: a[k].dtype for k in dtypes} == {k: np.dtype(v) for k, v in dtypes.items()}
+
+
+def test_decode_metadata_rejects_a_sequence_without_blocks():
+    from kavor_b200.engine.model_runner import decode_metadata
+
+    seqs = [SimpleNamespace(num_tokens=5, last_token=1, block_table=[3]),
+            SimpleNamespace(num_tokens=2, last_token=1, block_table=[])]
+    with pytest.raises(ValueError, match="needs a block"):
+        decode_metadata(seqs, 256)
+    empty = decode_metadata([], 256)
+    assert all(v.shape[0] == 0 for v in empty.values())
 
 
 class _Len(SimpleNamespace):

@@ -72,6 +72,10 @@ def test_reference_arm_line(monkeypatch, capsys):
     assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert "ramp fills" in line["cpu_baseline"]["sample"]
+    # ms_per_step is the work each step ran (one layer + the LM head), so steps x ms_per_step
+    # matches the run's clock; the value is the extrapolated whole step's throughput
+    assert 0 < line["ms_per_step"] < line["ms_per_step_extrapolated"]
+    assert line["value"] == pytest.approx(4 / (line["ms_per_step_extrapolated"] / 1e3))
 
 
 def test_teardown_guard_is_cancelled_in_time():

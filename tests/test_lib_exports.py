@@ -192,3 +192,10 @@ def test_clearing_device_error_bits_runs_the_reset_hooks(monkeypatch):
     word["bits"] = 4
     assert _lib.device_error(clear=False) == 4 and seen == []  # read only: nothing is reset
     assert _lib.device_error(clear=True) == 4 and seen == [4]
+
+
+def test_every_entry_point_has_an_integration_entry():
+    """Each declared entry point appears in the integration guide (its reference
+    call site or its use), so the guide covers the whole boundary."""
+    guide = (ROOT / "INTEGRATION.md").read_text()
+    assert sorted(n for n in _declared() if n not in guide) == []

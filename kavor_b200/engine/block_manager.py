@@ -134,10 +134,10 @@ class BlockManager:
         seq.block_table.clear()
 
     def can_append_block(self, seq: Sequence) -> bool:
-        return len(self.free_block_ids) >= (len(seq) % self.block_size == 1)
+        return len(self.free_block_ids) >= (seq.num_tokens % self.block_size == 1)
 
     def may_append_block(self, seq: Sequence) -> None:
-        if len(seq) % self.block_size == 1:
+        if seq.num_tokens % self.block_size == 1:
             seq.block_table.append(self.allocate_block())
 
     def may_append_blocks(self, seqs: list[Sequence]) -> None:

@@ -525,10 +525,10 @@ def run_ours(args) -> int:
         sample = CpuDecodeSample(shape, B, ctx0, threads)
         t_step = statistics.median(sample.step_time() for _ in range(5))
         cpu = {"value": B / t_step, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"5 sampled decode steps (B={B}, ctx={ctx0}): each 1 timed decoder layer of "
-                         f"{shape['num_hidden_layers']} + 1 LM-head GEMM on the CPU oracle, extrapolated "
-                         f"x{shape['num_hidden_layers']}; weights and KV pages are deterministic ramp fills "
-                         f"(the CPU time does not depend on the values)",
+               "sample": f"5 sampled decode steps (B={B}, ctx={ctx0}), median: each 1 timed decoder layer of "
+                         f"{shape['num_hidden_layers']} + 1 timed LM-head GEMM on the CPU oracle, the layer's time "
+                         f"extrapolated x{shape['num_hidden_layers']}; weights and KV pages are deterministic ramp "
+                         f"fills (the CPU time does not depend on the values)",
                "ms_per_step": t_step * 1e3}
 
     # the pipelined e2e beside the synchronous one (one GPU, no collectives; a failure is reported, not raised)
